@@ -1,0 +1,587 @@
+// dak_attention.cu - split-KV decode attention over KV that lives partly in
+// pinned host memory and partly in HBM, merged with log-sum-exp.
+//
+// Replaces opt_attention_decode_kernel / opt_attention_reduce_splits_kernel
+// (opt_attention/csrc/opt_attention_kernel.cuh:260-386) and their launcher
+// (opt_attention_kernel.cu:9-35).  The reference runs one CTA per
+// (batch, query head, split) and so re-reads every K/V byte once per query
+// head; it supports MHA, head_dim 128 and a per-batch-row host/device choice.
+// Here:
+//   * one CTA per (batch, KV head, split) serves all G = Hq/Hkv query heads of
+//     the GQA group, so every KV byte crosses the host link or HBM once;
+//   * K/V arrive as 64-token chunks through a 4-stage ring filled by TMA 4-D
+//     tile loads (128-byte swizzle) issued by one producer warp; each chunk is
+//     made of pages (64 tokens of one row in the reference's [B, H, S, D]
+//     layout, or page_size-token pages of a paged pool), and each page picks
+//     the host or the device tile map, so one sequence may span both tiers;
+//   * 4 compute warps do FP32 q.k, an online softmax (expf) and p.V on CUDA
+//     cores (the kernel is bound by memory, not math);
+//   * per-split (o, m, l) go to caller-provided FP32 scratch and a second
+//     kernel merges the splits with log-sum-exp, as kernel.cuh:362-386 does.
+#include <cfloat>
+
+#include "dak_common.cuh"
+#include "dak_host.h"
+
+namespace dak {
+
+namespace {
+
+constexpr int kHeadDim = 128;
+constexpr int kChunk = 64;          // tokens per pipeline stage
+constexpr int kAttnStages = 4;
+constexpr int kAttnComputeWarps = 4;
+constexpr int kAttnThreads = (kAttnComputeWarps + 1) * 32;
+constexpr int kMaxGroup = 8;
+constexpr uint32_t kHalfBox = kChunk * 128;              // 64 tokens x 64 dims x 2 B = 8 KB
+constexpr uint32_t kKvChunkBytes = 2 * kHalfBox;        // 16 KB for K (or V)
+constexpr uint32_t kStageBytes = 2 * kKvChunkBytes;     // K + V = 32 KB
+
+struct alignas(64) AttnParams {
+  CUtensorMap kmap[2];  // [0] host tier, [1] device tier; dims {128, rows, Hkv, n}
+  CUtensorMap vmap[2];
+  const void *query;
+  long long q_stride_b, q_stride_h;
+  const float *mask;
+  long long mask_stride_b;
+  void *out;
+  long long o_stride_b, o_stride_h;
+  float *partial_o;
+  float *partial_ml;
+  const int *block_table;  // paged mode; nullptr in batch-split mode
+  long long bt_stride;
+  const int *seq_lens;     // paged mode
+  int batch, host_size, num_q_heads, num_kv_heads, seq_len, split_size, num_splits, page_size;
+  float scaling;
+  int *status;
+};
+
+struct AttnSmem {
+  static constexpr uint32_t kv_off = 0;
+  static constexpr uint32_t q_off = kv_off + kAttnStages * kStageBytes;      // G x 128 fp32
+  static constexpr uint32_t p_off = q_off + kMaxGroup * kHeadDim * 4;         // 64 x G fp32
+  static constexpr uint32_t redmax_off = p_off + kChunk * kMaxGroup * 4;      // 2 x 4 x G
+  static constexpr uint32_t ored_off = redmax_off + 2 * kAttnComputeWarps * kMaxGroup * 4;  // 4 x G x 128
+  static constexpr uint32_t lred_off = ored_off + kAttnComputeWarps * kMaxGroup * kHeadDim * 4;
+  static constexpr uint32_t bar_off = lred_off + kAttnComputeWarps * kMaxGroup * 4;
+  static constexpr uint32_t flag_off = bar_off + 2 * kAttnStages * 8;
+  static constexpr uint32_t bytes = flag_off + 16 + 1024;
+};
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                            int c3, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// Where page j (page_size tokens) of sequence b lives: tier (0 host, 1 device),
+// the row offset inside the tile map's second dimension and the slab index
+// (4th dimension).
+struct PageLoc {
+  int tier, row, slab;
+};
+
+__device__ __forceinline__ PageLoc locate(const AttnParams &p, int b, int tok0) {
+  PageLoc l;
+  if (p.block_table) {
+    const int v = p.block_table[(long long)b * p.bt_stride + tok0 / p.page_size];
+    l.tier = v < 0 ? 0 : 1;
+    l.slab = v < 0 ? (-1 - v) : v;
+    l.row = 0;
+  } else {
+    l.tier = b < p.host_size ? 0 : 1;
+    l.slab = b < p.host_size ? b : b - p.host_size;
+    l.row = tok0;
+  }
+  return l;
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+  const uint32_t sbase = smem_u32(smem);
+  using S = AttnSmem;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int split = blockIdx.x % p.num_splits;
+  const int kvh = (blockIdx.x / p.num_splits) % p.num_kv_heads;
+  const int b = blockIdx.x / (p.num_splits * p.num_kv_heads);
+  const int seq = p.seq_lens ? min(p.seq_lens[b], p.seq_len) : p.seq_len;
+  const int t_begin = split * p.split_size;
+  const int t_end = min(seq, t_begin + p.split_size);
+  const int nchunks = t_end > t_begin ? (t_end - t_begin + kChunk - 1) / kChunk : 0;
+
+  float *q_s = reinterpret_cast<float *>(smem + S::q_off);
+  float *p_s = reinterpret_cast<float *>(smem + S::p_off);
+  float *redmax = reinterpret_cast<float *>(smem + S::redmax_off);
+  float *ored = reinterpret_cast<float *>(smem + S::ored_off);
+  float *lred = reinterpret_cast<float *>(smem + S::lred_off);
+  const uint32_t full0 = sbase + S::bar_off;
+  const uint32_t empty0 = full0 + kAttnStages * 8;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::flag_off);
+  const WaitCtx wc{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAttnStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kAttnComputeWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  // Query heads kvh*G .. kvh*G+G-1 (repeat_kv order) into shared memory as FP32.
+  for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x) {
+    const int g = i / kHeadDim, d = i % kHeadDim;
+    const uint16_t *q = reinterpret_cast<const uint16_t *>(p.query) + (long long)b * p.q_stride_b +
+                        (long long)(kvh * G + g) * p.q_stride_h;
+    q_s[g * kHeadDim + d] = Elem<T>::to_float(q[d]);
+  }
+  __syncthreads();
+
+  if (warp == kAttnComputeWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && nchunks > 0) {
+      for (int t = 0; t < 2; ++t) {
+        prefetch_tensormap(&p.kmap[t]);
+        prefetch_tensormap(&p.vmap[t]);
+      }
+      const uint64_t pol = l2_policy_evict_first();
+      const int psz = p.block_table ? p.page_size : kChunk;
+      uint32_t issued_mask = 0, issued_par = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kAttnStages;
+        const uint32_t ph = (uint32_t)((c / kAttnStages) & 1);
+        if (!mbar_wait<false>(empty0 + 8 * s, ph ^ 1u, wc)) break;
+        const int c0 = t_begin + c * kChunk;
+        const int valid = min(kChunk, t_end - c0);
+        const int npages = (valid + psz - 1) / psz;
+        const uint32_t fb = full0 + 8 * s;
+        mbar_arrive_expect_tx(fb, (uint32_t)npages * (uint32_t)psz * 128u * 4u);
+        const uint32_t kdst = sbase + S::kv_off + s * kStageBytes;
+        const uint32_t vdst = kdst + kKvChunkBytes;
+        for (int pg = 0; pg < npages; ++pg) {
+          const PageLoc loc = locate(p, b, c0 + pg * psz);
+          const uint32_t row_off = (uint32_t)(pg * psz) * 128u;
+          for (int h = 0; h < 2; ++h) {
+            tma_load_4d(kdst + h * kHalfBox + row_off, &p.kmap[loc.tier], h * 64, loc.row, kvh, loc.slab, fb, pol);
+            tma_load_4d(vdst + h * kHalfBox + row_off, &p.vmap[loc.tier], h * 64, loc.row, kvh, loc.slab, fb, pol);
+          }
+        }
+        issued_mask |= 1u << s;
+        issued_par = (issued_par & ~(1u << s)) | (ph << s);
+      }
+      if (*abort_flag) {
+        const WaitCtx drain{reinterpret_cast<volatile int *>(smem + S::flag_off + 4), p.status};
+        *drain.abort = 0;
+        for (int st = 0; st < kAttnStages; ++st)
+          if (issued_mask & (1u << st)) mbar_wait<false>(full0 + 8 * st, (issued_par >> st) & 1u, drain);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+
+  // ---------------------------------------------------------------- compute
+  const int tid = threadIdx.x;          // 0..127
+  const int qt = tid >> 1;              // q.k: token of this thread
+  const int qh = tid & 1;               //      and which 64-dim half
+  const int vd = 4 * lane;              // p.V: 4 dims d0..d0+3 of this thread
+  const int vh = vd >> 6;               //      their 64-dim box
+  const int vc = (vd & 63) >> 3;        //      logical 16-byte chunk in the box row
+  const int vw = (vd & 7) * 2;          //      byte offset inside the chunk
+  float m_run[G], l_part[G], o[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m_run[g] = -FLT_MAX;
+    l_part[g] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[g][j] = 0.f;
+  }
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int s = c % kAttnStages;
+    const uint32_t ph = (uint32_t)((c / kAttnStages) & 1);
+    const bool ok = mbar_wait<false>(full0 + 8 * s, ph, wc);
+    const uint8_t *kst = smem + S::kv_off + s * kStageBytes;
+    const uint8_t *vst = kst + kKvChunkBytes;
+    const int c0 = t_begin + c * kChunk;
+    const int valid = ok ? min(kChunk, t_end - c0) : 0;
+
+    // ---- scores for token qt, dims qh*64 .. qh*64+63
+    float sc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) sc[g] = 0.f;
+    if (qt < valid) {
+      const uint8_t *krow = kst + qh * kHalfBox + qt * 128;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint4 kv = *reinterpret_cast<const uint4 *>(krow + ((cc ^ (qt & 7)) << 4));
+        const float2 k0 = Elem<T>::to_float2(kv.x), k1 = Elem<T>::to_float2(kv.y);
+        const float2 k2 = Elem<T>::to_float2(kv.z), k3 = Elem<T>::to_float2(kv.w);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4 *>(q_s + g * kHeadDim + qh * 64 + cc * 8);
+          const float4 qb = *reinterpret_cast<const float4 *>(q_s + g * kHeadDim + qh * 64 + cc * 8 + 4);
+          float a = sc[g];
+          a = fmaf(qa.x, k0.x, a); a = fmaf(qa.y, k0.y, a); a = fmaf(qa.z, k1.x, a); a = fmaf(qa.w, k1.y, a);
+          a = fmaf(qb.x, k2.x, a); a = fmaf(qb.y, k2.y, a); a = fmaf(qb.z, k3.x, a); a = fmaf(qb.w, k3.y, a);
+          sc[g] = a;
+        }
+      }
+    }
+    const float mval = (p.mask && qt < valid) ? p.mask[(long long)b * p.mask_stride_b + c0 + qt] : 0.f;
+    float wmax[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float v = sc[g] + __shfl_xor_sync(0xffffffffu, sc[g], 1);
+      v = qt < valid ? v * p.scaling + mval : -FLT_MAX;
+      sc[g] = v;
+      float mx = v;
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      wmax[g] = mx;
+    }
+    float *rm = redmax + (c & 1) * kAttnComputeWarps * kMaxGroup;
+    if (lane == 0)
+#pragma unroll
+      for (int g = 0; g < G; ++g) rm[warp * kMaxGroup + g] = wmax[g];
+    named_sync(1, kAttnComputeWarps * 32);
+
+    // ---- online softmax update
+    float alpha[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mc = rm[g];
+#pragma unroll
+      for (int w = 1; w < kAttnComputeWarps; ++w) mc = fmaxf(mc, rm[w * kMaxGroup + g]);
+      const float mn = fmaxf(m_run[g], mc);
+      alpha[g] = (m_run[g] == -FLT_MAX) ? 0.f : expf(m_run[g] - mn);
+      const float pv = (qt < valid && mn != -FLT_MAX) ? expf(sc[g] - mn) : 0.f;
+      if (qh == 0) p_s[qt * kMaxGroup + g] = pv;
+      l_part[g] = l_part[g] * alpha[g] + (qh == 0 ? pv : 0.f);
+      m_run[g] = mn;
+    }
+    named_sync(1, kAttnComputeWarps * 32);
+
+    // ---- o += p . V over this warp's tokens (t = warp, warp+4, ...)
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[g][j] *= alpha[g];
+    for (int t = warp; t < valid; t += kAttnComputeWarps) {
+      const uint2 vv = *reinterpret_cast<const uint2 *>(vst + vh * kHalfBox + t * 128 + ((vc ^ (t & 7)) << 4) + vw);
+      const float2 v0 = Elem<T>::to_float2(vv.x), v1 = Elem<T>::to_float2(vv.y);
+      float pg[G];
+      if (G >= 4) {
+#pragma unroll
+        for (int g = 0; g < G; g += 4) {
+          const float4 pp = *reinterpret_cast<const float4 *>(p_s + t * kMaxGroup + g);
+          pg[g] = pp.x; pg[g + 1] = pp.y; pg[g + 2] = pp.z; pg[g + 3] = pp.w;
+        }
+      } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) pg[g] = p_s[t * kMaxGroup + g];
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        o[g][0] = fmaf(pg[g], v0.x, o[g][0]);
+        o[g][1] = fmaf(pg[g], v0.y, o[g][1]);
+        o[g][2] = fmaf(pg[g], v1.x, o[g][2]);
+        o[g][3] = fmaf(pg[g], v1.y, o[g][3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+  }
+
+  // ---- combine the 4 warps' partial o and the 128 threads' partial l
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float l = l_part[g];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    l += __shfl_xor_sync(0xffffffffu, l, 4);
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+    if (lane == 0) lred[warp * kMaxGroup + g] = l;
+    *reinterpret_cast<float4 *>(ored + (warp * kMaxGroup + g) * kHeadDim + vd) =
+        make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+  }
+  named_sync(1, kAttnComputeWarps * 32);
+  // Thread tid finishes dim (tid) of every head.
+  const int d = tid;
+  for (int g = 0; g < G; ++g) {
+    float acc = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnComputeWarps; ++w) {
+      acc += ored[(w * kMaxGroup + g) * kHeadDim + d];
+      l += lred[w * kMaxGroup + g];
+    }
+    const int hq = kvh * G + g;
+    if (p.num_splits == 1) {
+      uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + (long long)b * p.o_stride_b + (long long)hq * p.o_stride_h;
+      out[d] = Elem<T>::from_float(l == 0.f ? 0.f : acc / l);
+    } else {
+      const long long base = ((long long)b * p.num_q_heads + hq) * p.num_splits + split;
+      p.partial_o[base * kHeadDim + d] = acc;
+      if (d == 0) {
+        p.partial_ml[base * 2] = m_run[g];
+        p.partial_ml[base * 2 + 1] = l;
+      }
+    }
+  }
+}
+
+// Log-sum-exp merge of the splits (opt_attention_kernel.cuh:362-386).
+template <typename T>
+__global__ void __launch_bounds__(kHeadDim) attn_merge_kernel(const __grid_constant__ AttnParams p) {
+  const int hq = blockIdx.x % p.num_q_heads;
+  const int b = blockIdx.x / p.num_q_heads;
+  const int d = threadIdx.x;
+  const long long base = ((long long)b * p.num_q_heads + hq) * p.num_splits;
+  float gm = -FLT_MAX;
+  for (int s = 0; s < p.num_splits; ++s) gm = fmaxf(gm, p.partial_ml[(base + s) * 2]);
+  float den = 0.f, acc = 0.f;
+  for (int s = 0; s < p.num_splits; ++s) {
+    const float m = p.partial_ml[(base + s) * 2];
+    const float l = p.partial_ml[(base + s) * 2 + 1];
+    const float sc = (m == -FLT_MAX || gm == -FLT_MAX) ? 0.f : expf(m - gm);
+    den += l * sc;
+    acc += p.partial_o[(base + s) * kHeadDim + d] * sc;
+  }
+  uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + (long long)b * p.o_stride_b + (long long)hq * p.o_stride_h;
+  out[d] = Elem<T>::from_float(den == 0.f ? 0.f : acc / den);
+}
+
+template <typename T, int G>
+cudaError_t launch_g(const AttnParams &p, cudaStream_t stream) {
+  auto kern = attn_decode_kernel<T, G>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AttnSmem::bytes);
+  if (e != cudaSuccess) return e;
+  const int grid = p.batch * p.num_kv_heads * p.num_splits;
+  kern<<<grid, kAttnThreads, AttnSmem::bytes, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || p.num_splits == 1) return e;
+  attn_merge_kernel<T><<<p.batch * p.num_q_heads, kHeadDim, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_t(const AttnParams &p, int group, cudaStream_t stream) {
+  switch (group) {
+    case 1: return launch_g<T, 1>(p, stream);
+    case 2: return launch_g<T, 2>(p, stream);
+    case 4: return launch_g<T, 4>(p, stream);
+    case 8: return launch_g<T, 8>(p, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// 4-D tile map over K or V: dims {128, rows, Hkv, slabs}; box {64, box_rows, 1, 1}.
+int kv_map(CUtensorMap *out, const void *base, int dtype, long long rows, long long heads, long long slabs,
+           long long stride_row, long long stride_head, long long stride_slab, int box_rows);
+
+}  // namespace
+
+}  // namespace dak
+
+// ------------------------------------------------------------------ C ABI
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+namespace dak {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int kv_map(CUtensorMap *out, const void *base, int dtype, long long rows, long long heads, long long slabs,
+           long long stride_row, long long stride_head, long long stride_slab, int box_rows) {
+  int st = check_gpu_accessible(base, "KV");
+  if (st) return st;
+  auto fn = attn_encode_fn();
+  if (!fn) return fail(DAK_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t gdim[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)slabs};
+  const cuuint64_t gstride[3] = {(cuuint64_t)stride_row * 2u, (cuuint64_t)stride_head * 2u,
+                                 (cuuint64_t)stride_slab * 2u};
+  const cuuint32_t box[4] = {64u, (cuuint32_t)box_rows, 1u, 1u};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(out, dtype == DAK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  4, const_cast<void *>(base), gdim, gstride, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DAK_ERR_DRIVER, "cuTensorMapEncodeTiled (KV) failed with %d", (int)r);
+  return DAK_OK;
+}
+
+int check_kv_strides(const void *ptr, long long sb, long long sh, const char *what) {
+  if (!ptr) return fail(DAK_ERR_INVALID_ARG, "%s is null", what);
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return fail(DAK_ERR_ALIGNMENT, "%s must be 16-byte aligned", what);
+  if (sb <= 0 || sh <= 0 || (sb % 8) != 0 || (sh % 8) != 0)
+    return fail(DAK_ERR_ALIGNMENT, "%s batch/head strides must be positive multiples of 8 elements", what);
+  return DAK_OK;
+}
+
+int common_checks(int batch, int hq, int hkv, int head_dim, int split_size, int dtype, int *group) {
+  if (dtype != DAK_DTYPE_F16 && dtype != DAK_DTYPE_BF16)
+    return fail(DAK_ERR_UNSUPPORTED, "attention supports float16 and bfloat16 only");
+  if (head_dim != kHeadDim) return fail(DAK_ERR_UNSUPPORTED, "decode kernel requires head_dim == 128");
+  if (batch <= 0 || hq <= 0 || hkv <= 0) return fail(DAK_ERR_INVALID_ARG, "batch and head counts must be positive");
+  if (hq % hkv != 0) return fail(DAK_ERR_INVALID_ARG, "num_q_heads must be a multiple of num_kv_heads");
+  const int g = hq / hkv;
+  if (g != 1 && g != 2 && g != 4 && g != 8)
+    return fail(DAK_ERR_UNSUPPORTED, "query heads per KV head must be 1, 2, 4 or 8 (got %d)", g);
+  if (split_size <= 0 || split_size % kChunk != 0)
+    return fail(DAK_ERR_INVALID_ARG, "split_size must be a positive multiple of 64");
+  *group = g;
+  return DAK_OK;
+}
+
+}  // namespace
+}  // namespace dak
+
+using namespace dak;
+
+extern "C" {
+
+int dak_attn_decode(const dak_attn_decode_args *a, void *stream) {
+  if (!a) return fail(DAK_ERR_INVALID_ARG, "args is null");
+  int group, st;
+  if ((st = common_checks(a->batch, a->num_q_heads, a->num_kv_heads, a->head_dim, a->split_size, a->dtype, &group)))
+    return st;
+  if (a->host_size < 0 || a->host_size > a->batch)
+    return fail(DAK_ERR_INVALID_ARG, "host_size must be in [0, batch_size], got %d for batch_size=%d", a->host_size,
+                a->batch);
+  if (a->seq_len <= 0) return fail(DAK_ERR_INVALID_ARG, "seq_len must be positive");
+  if (!a->query || !a->out) return fail(DAK_ERR_INVALID_ARG, "query and out are required");
+  const int gpu_batch = a->batch - a->host_size;
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (gpu_batch > 0) {
+    if ((st = check_kv_strides(a->key, a->kv_stride_b, a->kv_stride_h, "key"))) return st;
+    if ((st = check_kv_strides(a->value, a->kv_stride_b, a->kv_stride_h, "value"))) return st;
+    if ((st = kv_map(&p.kmap[1], a->key, a->dtype, a->seq_len, a->num_kv_heads, gpu_batch, kHeadDim, a->kv_stride_h,
+                     a->kv_stride_b, kChunk)))
+      return st;
+    if ((st = kv_map(&p.vmap[1], a->value, a->dtype, a->seq_len, a->num_kv_heads, gpu_batch, kHeadDim,
+                     a->kv_stride_h, a->kv_stride_b, kChunk)))
+      return st;
+  }
+  if (a->host_size > 0) {
+    if ((st = check_kv_strides(a->key_host, a->kvh_stride_b, a->kvh_stride_h, "key_host"))) return st;
+    if ((st = check_kv_strides(a->value_host, a->kvh_stride_b, a->kvh_stride_h, "value_host"))) return st;
+    if ((st = kv_map(&p.kmap[0], a->key_host, a->dtype, a->seq_len, a->num_kv_heads, a->host_size, kHeadDim,
+                     a->kvh_stride_h, a->kvh_stride_b, kChunk)))
+      return st;
+    if ((st = kv_map(&p.vmap[0], a->value_host, a->dtype, a->seq_len, a->num_kv_heads, a->host_size, kHeadDim,
+                     a->kvh_stride_h, a->kvh_stride_b, kChunk)))
+      return st;
+  }
+  const int splits = (a->seq_len + a->split_size - 1) / a->split_size;
+  if (splits > 1 && (!a->partial_o || !a->partial_ml))
+    return fail(DAK_ERR_INVALID_ARG, "partial_o and partial_ml scratch are required when seq_len > split_size");
+  p.query = a->query;
+  p.q_stride_b = a->q_stride_b;
+  p.q_stride_h = a->q_stride_h;
+  p.mask = a->mask;
+  p.mask_stride_b = a->mask_stride_b;
+  p.out = a->out;
+  p.o_stride_b = a->o_stride_b;
+  p.o_stride_h = a->o_stride_h;
+  p.partial_o = a->partial_o;
+  p.partial_ml = a->partial_ml;
+  p.batch = a->batch;
+  p.host_size = a->host_size;
+  p.num_q_heads = a->num_q_heads;
+  p.num_kv_heads = a->num_kv_heads;
+  p.seq_len = a->seq_len;
+  p.split_size = a->split_size;
+  p.num_splits = splits;
+  p.page_size = kChunk;
+  p.scaling = a->scaling;
+  p.status = device_status_word();
+  if (!p.status) return fail(DAK_ERR_CUDA, "no device status word");
+  cudaError_t e = a->dtype == DAK_DTYPE_F16 ? launch_t<__half>(p, group, static_cast<cudaStream_t>(stream))
+                                            : launch_t<__nv_bfloat16>(p, group, static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "attention launch");
+}
+
+int dak_attn_decode_paged(const dak_attn_paged_args *a, void *stream) {
+  if (!a) return fail(DAK_ERR_INVALID_ARG, "args is null");
+  int group, st;
+  if ((st = common_checks(a->batch, a->num_q_heads, a->num_kv_heads, a->head_dim, a->split_size, a->dtype, &group)))
+    return st;
+  if (a->page_size != 16 && a->page_size != 32 && a->page_size != 64)
+    return fail(DAK_ERR_UNSUPPORTED, "page_size must be 16, 32 or 64");
+  if (a->max_seq_len <= 0 || !a->block_table || !a->seq_lens || a->bt_stride <= 0)
+    return fail(DAK_ERR_INVALID_ARG, "block_table, seq_lens and max_seq_len are required");
+  if ((long long)a->bt_stride * a->page_size < a->max_seq_len)
+    return fail(DAK_ERR_INVALID_ARG, "block_table rows are shorter than max_seq_len pages");
+  if (!a->query || !a->out) return fail(DAK_ERR_INVALID_ARG, "query and out are required");
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  const long long hs = (long long)a->page_size * kHeadDim;      // head stride in a page
+  const long long ps = hs * a->num_kv_heads;                     // page stride
+  // The pools' page counts are not passed; the maps cover the largest page
+  // index a 31-bit table entry can name.
+  const long long max_pages = 1ll << 24;
+  const void *pools[4] = {a->k_pool_host, a->v_pool_host, a->k_pool_dev, a->v_pool_dev};
+  for (int i = 0; i < 4; ++i) {
+    if (!pools[i]) continue;
+    if ((reinterpret_cast<uintptr_t>(pools[i]) & 15u) != 0) return fail(DAK_ERR_ALIGNMENT, "KV pools must be 16-byte aligned");
+    CUtensorMap *m = (i % 2 == 0) ? &p.kmap[i / 2] : &p.vmap[i / 2];
+    if ((st = kv_map(m, pools[i], a->dtype, a->page_size, a->num_kv_heads, max_pages, kHeadDim, hs, ps, a->page_size)))
+      return st;
+  }
+  if (!a->k_pool_dev && !a->k_pool_host) return fail(DAK_ERR_INVALID_ARG, "no KV pool given");
+  const int splits = (a->max_seq_len + a->split_size - 1) / a->split_size;
+  if (splits > 1 && (!a->partial_o || !a->partial_ml))
+    return fail(DAK_ERR_INVALID_ARG, "partial_o and partial_ml scratch are required when max_seq_len > split_size");
+  p.query = a->query;
+  p.q_stride_b = a->q_stride_b;
+  p.q_stride_h = a->q_stride_h;
+  p.out = a->out;
+  p.o_stride_b = a->o_stride_b;
+  p.o_stride_h = a->o_stride_h;
+  p.partial_o = a->partial_o;
+  p.partial_ml = a->partial_ml;
+  p.block_table = a->block_table;
+  p.bt_stride = a->bt_stride;
+  p.seq_lens = a->seq_lens;
+  p.batch = a->batch;
+  p.host_size = 0;
+  p.num_q_heads = a->num_q_heads;
+  p.num_kv_heads = a->num_kv_heads;
+  p.seq_len = a->max_seq_len;
+  p.split_size = a->split_size;
+  p.num_splits = splits;
+  p.page_size = a->page_size;
+  p.scaling = a->scaling;
+  p.status = device_status_word();
+  if (!p.status) return fail(DAK_ERR_CUDA, "no device status word");
+  cudaError_t e = a->dtype == DAK_DTYPE_F16 ? launch_t<__half>(p, group, static_cast<cudaStream_t>(stream))
+                                            : launch_t<__nv_bfloat16>(p, group, static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "paged attention launch");
+}
+
+}  // extern "C"

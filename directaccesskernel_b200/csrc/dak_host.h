@@ -1,0 +1,35 @@
+// dak_host.h - host-side declarations shared by the translation units of
+// libdak_b200.so (not part of the public C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "dak_linear.cuh"
+
+namespace dak {
+
+// Records a failure for dak_last_error_message() and returns `code`.
+int fail(int code, const char *fmt, ...);
+// Maps a CUDA runtime error to DAK_ERR_CUDA with its text (or DAK_OK).
+int cuda_status(cudaError_t e, const char *what);
+
+// Device address of the kernels' error word on the current device.
+int *device_status_word();
+// DAK_OK if `p` is memory of the current device or pinned host memory.
+int check_gpu_accessible(const void *p, const char *what);
+
+// Shared-memory bytes and launch of the CUDA-core kernel for `ntok_tmpl`
+// (1, 2, 4 or 8) tokens and dtype (DAK_DTYPE_F16 / _BF16).
+size_t linear_core_smem_bytes(int ntok_tmpl, int red_slots);
+cudaError_t launch_linear_core(const LinearParams &p, int ntok_tmpl, int dtype, int grid,
+                               int cluster, size_t smem, cudaStream_t stream);
+
+// Same for the tcgen05 kernel; `ntok_tmpl` is the UMMA N (multiple of 16).
+size_t linear_mma_smem_bytes(int ntok_tmpl, int red_slots);
+int linear_mma_stages(int ntok_tmpl, int ksplit);
+cudaError_t launch_linear_mma(const LinearParams &p, int ntok_tmpl, int dtype, int grid,
+                              int cluster, size_t smem, cudaStream_t stream);
+
+}  // namespace dak

@@ -1,0 +1,57 @@
+// dak_linear.cuh - launch parameters shared by the split-tier linear kernels.
+//
+// Data layout (kept from the reference, app/python/layers/linearLayer.py:226-229):
+// each tier holds the transposed weight Wt[K, cols] row-major, output features
+// contiguous, so one weight row segment of 64 features is 128 contiguous bytes.
+// The host tier lives in pinned, mapped host memory and is read by the GPU over
+// the host link; the device tier lives in HBM.  Both are streamed through the
+// same shared-memory ring by TMA tile loads, never staged through HBM.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace dak {
+
+constexpr int kBoxCols = 64;  // 64 x 16-bit = 128 B = one 128-byte swizzle span
+
+// ---- CUDA-core decode kernel (ntok <= 8) ---------------------------------
+constexpr int kCoreBN = 256;                      // output features per tile
+constexpr int kCoreBoxes = kCoreBN / kBoxCols;    // 4 TMA boxes per stage
+constexpr int kCoreBK = 32;                       // K rows per stage
+constexpr int kCoreStages = 8;                    // 8 x 16 KB weight stages
+constexpr int kCoreConsumerWarps = 8;
+constexpr int kCoreThreads = (kCoreConsumerWarps + 1) * 32;
+constexpr int kCoreMaxTok = 8;
+
+// ---- tcgen05 kernel (ntok up to 256) --------------------------------------
+constexpr int kMmaBM = 128;                       // UMMA M: output features per tile
+constexpr int kMmaBK = 64;                        // K rows per stage (4 x UMMA K=16)
+constexpr int kMmaMaxTok = 256;                   // UMMA N limit
+constexpr int kMmaEpiWarps = 4;
+constexpr int kMmaThreads = (2 + kMmaEpiWarps) * 32;  // producer, MMA, 4 epilogue
+
+struct alignas(64) LinearTier {
+  CUtensorMap wmap;  // Wt[K, cols]; box {64, BK}; 128-byte swizzle
+  int cols;          // output features of this tier
+  int col_offset;    // first output column of this tier in y
+  int cta_begin;     // CTAs [cta_begin, cta_begin + cta_count) serve this tier
+  int cta_count;
+  int ksplit;        // CTAs (consecutive, same cluster) sharing one tile along K
+  int pad_[3];
+};
+
+struct alignas(64) LinearParams {
+  LinearTier tier[2];  // [0] host tier, [1] device tier
+  CUtensorMap xmap;    // x[ntok, K] activations
+  void *y;             // y[ntok, ldy]
+  long long ldy;
+  int ntok;
+  int K;
+  int *status;         // device error word
+  int red_slots;       // partial-sum slots reserved in shared memory (max ksplit - 1)
+  int stages;          // pipeline depth (tcgen05 kernel; sized to the shared memory left)
+  int pad_[2];
+};
+
+}  // namespace dak

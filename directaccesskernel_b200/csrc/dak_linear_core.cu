@@ -1,0 +1,329 @@
+// dak_linear_core.cu - split-tier offloaded linear for decode (ntok <= 8),
+// CUDA-core FP32 FMAs with warp-shuffle reductions.
+//
+// Replaces the reference's `gemv` / `gemv_horizontal` (include/task/gemv.cuh:
+// 267-452), which feed wgmma with FP16 accumulation on sm_90a.  Here:
+//   * one CTA = 1 producer warp + 8 consumer warps;
+//   * the producer streams 256-feature x 32-row weight tiles (4 TMA boxes of
+//     64 x 32, 128-byte swizzle) and the matching activation slice through an
+//     8-stage mbarrier ring; the host tier's CTAs read pinned host memory over
+//     the host link, the device tier's CTAs read HBM, in the same launch;
+//   * consumer warp w owns 32 features of the tile; lane (q, ro) = (lane & 3,
+//     lane >> 2) reads 16 bytes of rows ro, ro+8, ... and keeps FP32 partial
+//     sums for 8 features x NTOK tokens; a 3-step xor shuffle sums the 8 row
+//     groups (the warp-shuffle reduction);
+//   * tiles split along K over `ksplit` CTAs of one thread-block cluster are
+//     summed in the leader CTA's shared memory through DSMEM stores and
+//     remote mbarrier arrivals (no global scratch, no atomics);
+//   * the result is cast to 16-bit once and written with plain stores, so the
+//     output needs no zero fill (the reference reduce-adds into a zeroed C).
+#include "dak_common.cuh"
+#include "dak_host.h"
+#include "dak_linear.cuh"
+
+namespace dak {
+
+namespace {
+
+constexpr uint32_t kCoreWStageBytes = kCoreBN * kCoreBK * 2;   // 16 KB
+constexpr uint32_t kCoreBoxBytes = kBoxCols * kCoreBK * 2;     // 4 KB
+
+template <int NTOK>
+struct CoreLayout {
+  static constexpr uint32_t x_stage_bytes = NTOK * kCoreBK * 2;
+  static constexpr uint32_t x_stage_stride = (x_stage_bytes + 127) & ~127u;
+  static constexpr uint32_t w_off = 0;
+  static constexpr uint32_t x_off = w_off + kCoreStages * kCoreWStageBytes;
+  static constexpr uint32_t bar_off = x_off + kCoreStages * x_stage_stride;
+  // full[S], empty[S], red_full, red_free
+  static constexpr uint32_t nbars = 2 * kCoreStages + 2;
+  static constexpr uint32_t flag_off = bar_off + nbars * 8;
+  static constexpr uint32_t red_off = (flag_off + 16 + 15) & ~15u;
+  static constexpr uint32_t red_slot_floats = NTOK * kCoreBN;
+  static constexpr uint32_t bytes(int red_slots) {
+    return red_off + (uint32_t)red_slots * red_slot_floats * 4 + 1024;  // +1024: base alignment
+  }
+};
+
+template <typename T, int NTOK>
+__global__ void __launch_bounds__(kCoreThreads, 1)
+    linear_core_kernel(const __grid_constant__ LinearParams p) {
+  using L = CoreLayout<NTOK>;
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte-swizzled TMA destinations want 1024-byte alignment.
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+  const uint32_t sbase = smem_u32(smem);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  const int ti = (p.tier[1].cta_count > 0 && (int)blockIdx.x >= p.tier[1].cta_begin) ? 1 : 0;
+  const LinearTier &tier = p.tier[ti];
+  const int local = (int)blockIdx.x - tier.cta_begin;
+  const int ks = tier.ksplit;
+  const int groups = tier.cta_count / ks;
+  const int g = local / ks;
+  const int r = local - g * ks;
+  // CTAs that only pad the tier to a whole number of clusters do no work.
+  const bool idle = local >= tier.cta_count;
+  const int ntiles = (tier.cols + kCoreBN - 1) / kCoreBN;
+  const int nkb = (p.K + kCoreBK - 1) / kCoreBK;
+  const int kb0 = (int)((long long)r * nkb / ks);
+  const int kb1 = (int)((long long)(r + 1) * nkb / ks);
+
+  const uint32_t full0 = sbase + L::bar_off;
+  const uint32_t empty0 = full0 + kCoreStages * 8;
+  const uint32_t red_full = empty0 + kCoreStages * 8;
+  const uint32_t red_free = red_full + 8;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::flag_off);
+  float *red = reinterpret_cast<float *>(smem + L::red_off);
+  const WaitCtx wc{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kCoreStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kCoreConsumerWarps);
+    }
+    mbar_init(red_full, (uint32_t)(ks > 1 ? (ks - 1) * kCoreConsumerWarps * 32 : 1));
+    mbar_init(red_free, kCoreConsumerWarps);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  // Peers arrive on these barriers, so the whole cluster waits for the inits.
+  cluster_sync_all();
+
+  if (warp == kCoreConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && ntiles > 0) {
+      prefetch_tensormap(&tier.wmap);
+      prefetch_tensormap(&p.xmap);
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_mask = 0, issued_par = 0;  // last issued phase per stage
+      bool aborted = false;
+      for (int tile = idle ? ntiles : g; tile < ntiles && !aborted; tile += groups) {
+        const int nbox = min(kCoreBoxes, (tier.cols - tile * kCoreBN + kBoxCols - 1) / kBoxCols);
+        const uint32_t bytes = (uint32_t)nbox * kCoreBoxBytes + L::x_stage_bytes;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait<false>(empty0 + 8 * s, ph ^ 1u, wc)) {
+            aborted = true;
+            break;
+          }
+          const uint32_t fb = full0 + 8 * s;
+          mbar_arrive_expect_tx(fb, bytes);
+          const uint32_t wdst = sbase + L::w_off + s * kCoreWStageBytes;
+          for (int bx = 0; bx < nbox; ++bx)
+            tma_load_2d(wdst + bx * kCoreBoxBytes, &tier.wmap, tile * kCoreBN + bx * kBoxCols,
+                        kb * kCoreBK, fb, pol_w);
+          tma_load_2d(sbase + L::x_off + s * L::x_stage_stride, &p.xmap, kb * kCoreBK, 0, fb,
+                      pol_x);
+          issued_mask |= 1u << s;
+          issued_par = (issued_par & ~(1u << s)) | (ph << s);
+          if (++s == kCoreStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Let the copies already in flight land before the CTA can exit.
+        const WaitCtx drain{reinterpret_cast<volatile int *>(smem + L::flag_off + 4), p.status};
+        *drain.abort = 0;
+        for (int st = 0; st < kCoreStages; ++st)
+          if (issued_mask & (1u << st)) mbar_wait<false>(full0 + 8 * st, (issued_par >> st) & 1u, drain);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------- consumers
+    const int b = warp >> 1;         // TMA box (64 features) of this warp
+    const int q = lane & 3;          // 16-byte chunk within the warp's 64 bytes
+    const int ro = lane >> 2;        // row offset 0..7 inside each 8-row group
+    const int c = (warp & 1) * 4 + q;  // logical 16-byte chunk in the 128-byte row
+    const uint32_t chunk_off = (uint32_t)((c ^ ro) << 4);  // 128-byte swizzle: chunk ^ (row & 7)
+    const uint32_t my_rank = cluster_ctarank();
+    int s = 0;
+    uint32_t ph = 0;
+    int nred = 0;
+
+    for (int tile = idle ? ntiles : g; tile < ntiles; tile += groups) {
+      const int nbox = min(kCoreBoxes, (tier.cols - tile * kCoreBN + kBoxCols - 1) / kBoxCols);
+      const bool active = b < nbox;
+      float acc[NTOK][8];
+#pragma unroll
+      for (int t = 0; t < NTOK; ++t)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[t][j] = 0.f;
+
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const bool ok = mbar_wait<false>(full0 + 8 * s, ph, wc);
+        if (ok && active) {
+          const uint8_t *wst = smem + L::w_off + s * kCoreWStageBytes + b * kCoreBoxBytes;
+          const uint16_t *xst =
+              reinterpret_cast<const uint16_t *>(smem + L::x_off + s * L::x_stage_stride);
+#pragma unroll
+          for (int i = 0; i < kCoreBK / 8; ++i) {
+            const int row = ro + 8 * i;
+            const uint4 wv = *reinterpret_cast<const uint4 *>(wst + row * 128 + chunk_off);
+            float wf[8];
+            {
+              const float2 f0 = Elem<T>::to_float2(wv.x), f1 = Elem<T>::to_float2(wv.y);
+              const float2 f2 = Elem<T>::to_float2(wv.z), f3 = Elem<T>::to_float2(wv.w);
+              wf[0] = f0.x; wf[1] = f0.y; wf[2] = f1.x; wf[3] = f1.y;
+              wf[4] = f2.x; wf[5] = f2.y; wf[6] = f3.x; wf[7] = f3.y;
+            }
+#pragma unroll
+            for (int t = 0; t < NTOK; ++t) {
+              const float xv = Elem<T>::to_float(xst[t * kCoreBK + row]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[t][j] = fmaf(wf[j], xv, acc[t][j]);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
+        if (++s == kCoreStages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+
+      // Warp-shuffle reduction over the 8 row groups (lane bits 2..4).
+#pragma unroll
+      for (int t = 0; t < NTOK; ++t)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float v = acc[t][j];
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 16);
+          acc[t][j] = v;
+        }
+      // Lane (q, ro) now owns token ro of its 8 features.
+      float out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = 0.f;
+#pragma unroll
+      for (int t = 0; t < NTOK; ++t)
+        if (t == ro)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) out[j] = acc[t][j];
+
+      const int fcol = b * kBoxCols + c * 8;  // feature within the tile
+      bool write_out = true;
+      if (ks > 1) {
+        if (r > 0) {
+          // Member: push the partial into the leader's slot r-1.
+          if (nred > 0) mbar_wait<true>(red_free, (uint32_t)((nred - 1) & 1), wc);
+          const uint32_t leader = my_rank - (uint32_t)r;
+          if (ro < NTOK) {
+            const uint32_t dst = mapa_shared(
+                smem_u32(red + (size_t)(r - 1) * L::red_slot_floats + ro * kCoreBN + fcol), leader);
+            st_cluster_v4(dst, out[0], out[1], out[2], out[3]);
+            st_cluster_v4(dst + 16, out[4], out[5], out[6], out[7]);
+          }
+          mbar_arrive_remote(mapa_shared(red_full, leader));
+          write_out = false;
+        } else {
+          // Leader: add the members' partials once all of them have landed.
+          mbar_wait<true>(red_full, (uint32_t)(nred & 1), wc);
+          if (ro < NTOK) {
+            for (int m = 0; m < ks - 1; ++m) {
+              const float *src = red + (size_t)m * L::red_slot_floats + ro * kCoreBN + fcol;
+              const float4 a0 = *reinterpret_cast<const float4 *>(src);
+              const float4 a1 = *reinterpret_cast<const float4 *>(src + 4);
+              out[0] += a0.x; out[1] += a0.y; out[2] += a0.z; out[3] += a0.w;
+              out[4] += a1.x; out[5] += a1.y; out[6] += a1.z; out[7] += a1.w;
+            }
+          }
+          __syncwarp();
+          if (lane == 0)
+            for (int m = 1; m < ks; ++m) mbar_arrive_remote(mapa_shared(red_free, my_rank + m));
+        }
+        ++nred;
+      }
+
+      if (write_out && active && ro < p.ntok) {
+        const int col = tile * kCoreBN + fcol;
+        if (col < tier.cols) {
+          T *yrow = reinterpret_cast<T *>(p.y) + (long long)ro * p.ldy + tier.col_offset + col;
+          if (col + 8 <= tier.cols && (reinterpret_cast<uintptr_t>(yrow) & 15u) == 0) {
+            uint4 v;
+            v.x = Elem<T>::pack2(out[0], out[1]);
+            v.y = Elem<T>::pack2(out[2], out[3]);
+            v.z = Elem<T>::pack2(out[4], out[5]);
+            v.w = Elem<T>::pack2(out[6], out[7]);
+            *reinterpret_cast<uint4 *>(yrow) = v;
+          } else {
+            uint16_t *yr = reinterpret_cast<uint16_t *>(yrow);
+            for (int j = 0; j < 8 && col + j < tier.cols; ++j) yr[j] = Elem<T>::from_float(out[j]);
+          }
+        }
+      }
+    }
+  }
+  // No CTA leaves while a peer may still touch its shared memory.
+  cluster_sync_all();
+}
+
+template <typename T, int NTOK>
+cudaError_t launch_typed(const LinearParams &p, int grid, int cluster, size_t smem,
+                         cudaStream_t stream) {
+  auto kern = linear_core_kernel<T, NTOK>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  if (cluster > 8) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kCoreThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <typename T>
+cudaError_t launch_dtype(const LinearParams &p, int ntok_tmpl, int grid, int cluster, size_t smem,
+                         cudaStream_t stream) {
+  switch (ntok_tmpl) {
+    case 1: return launch_typed<T, 1>(p, grid, cluster, smem, stream);
+    case 2: return launch_typed<T, 2>(p, grid, cluster, smem, stream);
+    case 4: return launch_typed<T, 4>(p, grid, cluster, smem, stream);
+    case 8: return launch_typed<T, 8>(p, grid, cluster, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+size_t linear_core_smem_bytes(int ntok_tmpl, int red_slots) {
+  switch (ntok_tmpl) {
+    case 1: return CoreLayout<1>::bytes(red_slots);
+    case 2: return CoreLayout<2>::bytes(red_slots);
+    case 4: return CoreLayout<4>::bytes(red_slots);
+    case 8: return CoreLayout<8>::bytes(red_slots);
+    default: return 0;
+  }
+}
+
+cudaError_t launch_linear_core(const LinearParams &p, int ntok_tmpl, int dtype, int grid,
+                               int cluster, size_t smem, cudaStream_t stream) {
+  if (dtype == DAK_DTYPE_F16) return launch_dtype<__half>(p, ntok_tmpl, grid, cluster, smem, stream);
+  if (dtype == DAK_DTYPE_BF16)
+    return launch_dtype<__nv_bfloat16>(p, ntok_tmpl, grid, cluster, smem, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace dak

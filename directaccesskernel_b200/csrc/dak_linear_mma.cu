@@ -1,0 +1,451 @@
+// dak_linear_mma.cu - split-tier offloaded linear on the 5th-generation tensor
+// cores (tcgen05.mma kind::f16, FP32 accumulators in TMEM), for batched decode
+// and prefill (ntok 9..256).
+//
+// Replaces the reference's wgmma kernels `gemv_multicast`,
+// `gemv_horizontal_multicast` and their `_prefill` variants
+// (include/task/gemv_multicast.cuh:185-914), which multicast 64x64 weight
+// tiles to a 2-CTA cluster and accumulate in FP16.  Here the GEMM is "swap-AB":
+// 128 output features form the UMMA M dimension and the tokens the UMMA N
+// dimension (16..256), so one CTA applies each weight tile to all tokens and no
+// weight byte is fetched twice - no multicast is needed or used.
+//
+// Roles (192 threads): warp 0 issues TMA loads (two 64x64 weight boxes with
+// 128-byte swizzle, MN-major, plus the 64-wide activation slice, K-major, per
+// stage); warp 1 owns TMEM and issues the MMAs from one lane; warps 2..5 read
+// the accumulators back with tcgen05.ld (each warp its TMEM lane quadrant) and
+// write the 16-bit output.  Tiles split along K over `ksplit` CTAs of a cluster
+// are reduce-scattered through DSMEM: each CTA of the group owns 128/ksplit
+// features of the tile, receives the other CTAs' partials for them in its own
+// shared memory and writes them out.
+#include "dak_common.cuh"
+#include "dak_host.h"
+#include "dak_linear.cuh"
+
+#include <type_traits>
+
+namespace dak {
+
+namespace {
+
+constexpr uint32_t kMmaBoxBytes = kBoxCols * kMmaBK * 2;       // 8 KB (64 x 64)
+constexpr uint32_t kMmaWStageBytes = 2 * kMmaBoxBytes;         // 16 KB (128 x 64)
+constexpr int kMmaMaxKsplit = 4;
+constexpr int kMmaMaxStages = 8;
+constexpr uint32_t kSmemPerBlock = 227 * 1024;
+
+// Shared-memory layout; the pipeline depth is chosen at launch so that the
+// stages and the split-K receive buffer fit in one SM's shared memory.
+template <int NTOKP>
+struct MmaLayout {
+  static constexpr uint32_t x_stage_bytes = NTOKP * 128;  // NTOKP rows x 64 k x 2 B
+  static constexpr uint32_t red_row = NTOKP + 4;  // floats per feature row (padded)
+  int stages;
+  uint32_t w_off, x_off, bar_off, misc_off, red_off;
+  __host__ __device__ explicit MmaLayout(int s) : stages(s) {
+    w_off = 0;
+    x_off = w_off + (uint32_t)s * kMmaWStageBytes;
+    bar_off = x_off + (uint32_t)s * x_stage_bytes;
+    // full[S], empty[S], tmem_full[2], tmem_empty[2], red_full, red_free
+    misc_off = bar_off + (uint32_t)(2 * s + 6) * 8;  // tmem base slot, abort flags
+    red_off = (misc_off + 16 + 15) & ~15u;
+  }
+  __host__ __device__ static constexpr uint32_t red_floats(int ks) {
+    return ks > 1 ? (uint32_t)(ks - 1) * (uint32_t)(kMmaBM / ks) * red_row : 0u;
+  }
+  __host__ __device__ uint32_t bytes(int ks) const { return red_off + red_floats(ks) * 4 + 1024; }
+  __host__ __device__ static constexpr uint32_t tmem_cols() {
+    return (2 * NTOKP <= 32) ? 32 : (2 * NTOKP <= 64) ? 64 : (2 * NTOKP <= 128) ? 128
+           : (2 * NTOKP <= 256) ? 256 : 512;
+  }
+};
+
+// ------------------------------------------------------------- tcgen05 PTX
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2u << 61;  // layout: SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D F32, A/B 16-bit, A MN-major (features contiguous),
+// B K-major (activations), M = 128, N = ntokp.
+template <typename T>
+__host__ __device__ constexpr uint32_t mma_idesc(int ntokp) {
+  return (1u << 4)                                            // D format F32
+         | ((std::is_same<T, __half>::value ? 0u : 1u) << 7)   // A format F16/BF16
+         | ((std::is_same<T, __half>::value ? 0u : 1u) << 10)  // B format
+         | (1u << 15)                                          // A major: MN
+         | (0u << 16)                                          // B major: K
+         | ((uint32_t)(ntokp >> 3) << 17)                      // N >> 3
+         | ((uint32_t)(kMmaBM >> 4) << 24);                    // M >> 4
+}
+
+template <typename T, int NTOKP>
+__global__ void __launch_bounds__(kMmaThreads, 1)
+    linear_mma_kernel(const __grid_constant__ LinearParams p) {
+  const MmaLayout<NTOKP> L(p.stages);
+  const int S = L.stages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+  const uint32_t sbase = smem_u32(smem);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  const int ti = (p.tier[1].cta_count > 0 && (int)blockIdx.x >= p.tier[1].cta_begin) ? 1 : 0;
+  const LinearTier &tier = p.tier[ti];
+  const int local = (int)blockIdx.x - tier.cta_begin;
+  const int ks = tier.ksplit;
+  const int groups = tier.cta_count / ks;
+  const int g = local / ks;
+  const int r = local - g * ks;
+  // CTAs that only pad the tier to a whole number of clusters do no work.
+  const bool idle = local >= tier.cta_count;
+  const int ntiles = (tier.cols + kMmaBM - 1) / kMmaBM;
+  const int nkb = (p.K + kMmaBK - 1) / kMmaBK;
+  const int kb0 = (int)((long long)r * nkb / ks);
+  const int kb1 = (int)((long long)(r + 1) * nkb / ks);
+  const int feat_per_owner = kMmaBM / ks;  // features each CTA of the group writes
+
+  const uint32_t full0 = sbase + L.bar_off;
+  const uint32_t empty0 = full0 + S * 8;
+  const uint32_t tfull0 = empty0 + S * 8;
+  const uint32_t tempty0 = tfull0 + 16;
+  const uint32_t red_full = tempty0 + 16;
+  const uint32_t red_free = red_full + 8;
+  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(smem + L.misc_off);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.misc_off + 4);
+  float *red = reinterpret_cast<float *>(smem + L.red_off);
+  const WaitCtx wc{abort_flag, p.status};
+
+  // Owners receive (ks-1) senders x (4/ks) warps x 32 lanes arrivals per round;
+  // senders get one arrival from lane 0 of every owner warp of the other ranks.
+  const uint32_t red_full_count = ks > 1 ? (uint32_t)((ks - 1) * (kMmaEpiWarps / ks) * 32) : 1u;
+  const uint32_t red_free_count = ks > 1 ? (uint32_t)((ks - 1) * (kMmaEpiWarps / ks)) : 1u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, kMmaEpiWarps);
+    }
+    mbar_init(red_full, red_full_count);
+    mbar_init(red_free, red_free_count);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(sbase + L.misc_off, L.tmem_cols());
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && ntiles > 0 && kb1 > kb0) {
+      prefetch_tensormap(&tier.wmap);
+      prefetch_tensormap(&p.xmap);
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0, issued_mask = 0, issued_par = 0;
+      bool aborted = false;
+      for (int tile = idle ? ntiles : g; tile < ntiles && !aborted; tile += groups) {
+        const int nbox = min(2, (tier.cols - tile * kMmaBM + kBoxCols - 1) / kBoxCols);
+        const uint32_t bytes = (uint32_t)nbox * kMmaBoxBytes + L.x_stage_bytes;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait<false>(empty0 + 8 * s, ph ^ 1u, wc)) {
+            aborted = true;
+            break;
+          }
+          const uint32_t fb = full0 + 8 * s;
+          mbar_arrive_expect_tx(fb, bytes);
+          const uint32_t wdst = sbase + L.w_off + s * kMmaWStageBytes;
+          for (int bx = 0; bx < nbox; ++bx)
+            tma_load_2d(wdst + bx * kMmaBoxBytes, &tier.wmap, tile * kMmaBM + bx * kBoxCols,
+                        kb * kMmaBK, fb, pol_w);
+          tma_load_2d(sbase + L.x_off + s * L.x_stage_bytes, &p.xmap, kb * kMmaBK, 0, fb, pol_x);
+          issued_mask |= 1u << s;
+          issued_par = (issued_par & ~(1u << s)) | (ph << s);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag) {
+        const WaitCtx drain{reinterpret_cast<volatile int *>(smem + L.misc_off + 8), p.status};
+        *drain.abort = 0;
+        for (int st = 0; st < S; ++st)
+          if (issued_mask & (1u << st)) mbar_wait<false>(full0 + 8 * st, (issued_par >> st) & 1u, drain);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (ntiles > 0 && kb1 > kb0) {
+      constexpr uint32_t idesc = mma_idesc<T>(NTOKP);
+      int s = 0;
+      uint32_t ph = 0;
+      int n = 0;
+      for (int tile = idle ? ntiles : g; tile < ntiles; tile += groups, ++n) {
+        const int ab = n & 1;
+        const uint32_t use = (uint32_t)(n >> 1);
+        // Wait until the epilogue drained this accumulator buffer.
+        mbar_wait<false>(tempty0 + 8 * ab, (use & 1u) ^ 1u, wc);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(ab * NTOKP);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          const bool ok = mbar_wait<false>(full0 + 8 * s, ph, wc);
+          tc_fence_after();
+          if (lane == 0) {
+            if (ok) {
+              const uint32_t wst = sbase + L.w_off + s * kMmaWStageBytes;
+              const uint32_t xst = sbase + L.x_off + s * L.x_stage_bytes;
+#pragma unroll
+              for (int kk = 0; kk < kMmaBK / 16; ++kk) {
+                // A: MN-major SW128; 16 K rows = 2 KB; LBO = next 64-feature box, SBO = 8 rows.
+                const uint64_t ad = smem_desc_sw128(wst + kk * 2048, kMmaBoxBytes, 1024);
+                // B: K-major SW128; 16 K elements = 32 B inside the swizzle span; SBO = 8 rows.
+                const uint64_t bd = smem_desc_sw128(xst + kk * 32, 16, 1024);
+                tc_mma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            tc_commit(empty0 + 8 * s);  // frees the stage once these MMAs have read it
+          }
+          __syncwarp();
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (lane == 0) tc_commit(tfull0 + 8 * ab);
+        __syncwarp();
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int qd = warp & 3;                 // TMEM lane quadrant of this warp
+    const int f = qd * 32 + lane;            // feature within the 128-feature tile
+    const int owner = (qd * 32) / feat_per_owner;  // rank of the group that writes f
+    const uint32_t my_rank = cluster_ctarank();
+    const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
+    int n = 0;
+    int nred = 0;
+    if (kb1 > kb0) {
+      for (int tile = idle ? ntiles : g; tile < ntiles; tile += groups, ++n) {
+        const int ab = n & 1;
+        const uint32_t use = (uint32_t)(n >> 1);
+        mbar_wait<false>(tfull0 + 8 * ab, use & 1u, wc);
+        tc_fence_after();
+        const uint32_t acc_addr = tmem_base + lane_addr + (uint32_t)(ab * NTOKP);
+        const int col = tile * kMmaBM + f;
+        const bool col_ok = col < tier.cols;
+        T *ycol = reinterpret_cast<T *>(p.y) + tier.col_offset + col;
+
+        if (ks == 1 || owner == r) {
+          if (ks > 1) mbar_wait<true>(red_full, (uint32_t)(nred & 1), wc);
+          const int fl = f - owner * feat_per_owner;
+#pragma unroll 1
+          for (int c0 = 0; c0 < NTOKP; c0 += 32) {
+            float v[32];
+            tmem_ld32(acc_addr + (uint32_t)c0, v);
+            if (ks > 1) {
+              for (int m = 0; m < ks - 1; ++m) {
+                const float *src = red + ((size_t)m * feat_per_owner + fl) * L.red_row + c0;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                  const float4 a = *reinterpret_cast<const float4 *>(src + j);
+                  v[j] += a.x; v[j + 1] += a.y; v[j + 2] += a.z; v[j + 3] += a.w;
+                }
+              }
+            }
+            if (col_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (c0 + j < p.ntok)
+                  reinterpret_cast<uint16_t *>(ycol)[(long long)(c0 + j) * p.ldy] =
+                      Elem<T>::from_float(v[j]);
+            }
+          }
+          if (ks > 1) {
+            __syncwarp();
+            if (lane == 0)
+              for (int m = 0; m < ks; ++m)
+                if (m != r) mbar_arrive_remote(mapa_shared(red_free, my_rank - r + m));
+          }
+        } else {
+          // Sender: push this warp's partial to the owner of its features.
+          if (nred > 0) mbar_wait<true>(red_free, (uint32_t)((nred - 1) & 1), wc);
+          const int slot = r < owner ? r : r - 1;
+          const int fl = f - owner * feat_per_owner;
+          const uint32_t owner_rank = my_rank - r + owner;
+          const uint32_t dst_base = mapa_shared(
+              smem_u32(red + ((size_t)slot * feat_per_owner + fl) * L.red_row), owner_rank);
+#pragma unroll 1
+          for (int c0 = 0; c0 < NTOKP; c0 += 32) {
+            float v[32];
+            tmem_ld32(acc_addr + (uint32_t)c0, v);
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              st_cluster_v4(dst_base + (uint32_t)(c0 + j) * 4, v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+          mbar_arrive_remote(mapa_shared(red_full, owner_rank));
+        }
+        if (ks > 1) ++nred;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty0 + 8 * ab);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, L.tmem_cols());
+}
+
+template <typename T, int NTOKP>
+cudaError_t launch_typed(const LinearParams &p, int grid, int cluster, size_t smem,
+                         cudaStream_t stream) {
+  auto kern = linear_mma_kernel<T, NTOKP>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kMmaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <typename T>
+cudaError_t launch_dtype(const LinearParams &p, int ntokp, int grid, int cluster, size_t smem,
+                         cudaStream_t stream) {
+  switch (ntokp) {
+    case 16: return launch_typed<T, 16>(p, grid, cluster, smem, stream);
+    case 32: return launch_typed<T, 32>(p, grid, cluster, smem, stream);
+    case 64: return launch_typed<T, 64>(p, grid, cluster, smem, stream);
+    case 128: return launch_typed<T, 128>(p, grid, cluster, smem, stream);
+    case 256: return launch_typed<T, 256>(p, grid, cluster, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int NTOKP>
+int stages_for(int ks) {
+  int st = kMmaMaxStages;
+  while (st > 2 && MmaLayout<NTOKP>(st).bytes(ks) > kSmemPerBlock) --st;
+  return st;
+}
+
+template <int NTOKP>
+size_t smem_for(int ks) {
+  return MmaLayout<NTOKP>(stages_for<NTOKP>(ks)).bytes(ks);
+}
+
+}  // namespace
+
+int linear_mma_stages(int ntokp, int ksplit) {
+  switch (ntokp) {
+    case 16: return stages_for<16>(ksplit);
+    case 32: return stages_for<32>(ksplit);
+    case 64: return stages_for<64>(ksplit);
+    case 128: return stages_for<128>(ksplit);
+    case 256: return stages_for<256>(ksplit);
+    default: return 0;
+  }
+}
+
+// `red_slots` is the largest ksplit of the launch minus one.
+size_t linear_mma_smem_bytes(int ntokp, int red_slots) {
+  const int ks = red_slots + 1;
+  if (ks > kMmaMaxKsplit || (ks & (ks - 1)) != 0) return 0;
+  switch (ntokp) {
+    case 16: return smem_for<16>(ks);
+    case 32: return smem_for<32>(ks);
+    case 64: return smem_for<64>(ks);
+    case 128: return smem_for<128>(ks);
+    case 256: return smem_for<256>(ks);
+    default: return 0;
+  }
+}
+
+cudaError_t launch_linear_mma(const LinearParams &p, int ntokp, int dtype, int grid, int cluster,
+                              size_t smem, cudaStream_t stream) {
+  if (dtype == DAK_DTYPE_F16) return launch_dtype<__half>(p, ntokp, grid, cluster, smem, stream);
+  if (dtype == DAK_DTYPE_BF16)
+    return launch_dtype<__nv_bfloat16>(p, ntokp, grid, cluster, smem, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace dak

@@ -1,0 +1,260 @@
+/*
+ * dak_b200.h - C ABI of the B200 (sm_100a) direct-access offloading kernels.
+ *
+ * Everything here is plain C: pointers, sizes and status codes, no torch or
+ * pybind types.  A CUDA stream is passed as `void *` and must be a
+ * `cudaStream_t` (NULL = legacy default stream).  No entry point allocates
+ * device or host memory and none synchronizes the stream, so every launch can
+ * be captured into a CUDA graph.
+ *
+ * Reference interfaces replaced (paths inside shouxulin/DirectAccessKernel):
+ *   - src/torch_runtime.cu:120-468   pybind module `offload.runtime`
+ *   - src/runtime.cu:9-16            print_device_name
+ *   - include/task/utils.cuh:3-14    flush_l2_cache
+ *   - opt_attention/csrc/opt_attention_ext.cpp:164-337 and
+ *     opt_attention/csrc/opt_attention_kernel.cu:9-35   `opt_attention._C.decode`
+ *
+ * Every function returns DAK_OK (0) or a DAK_ERR_* code; dak_last_error_message()
+ * gives the detail text of the calling thread's last failure.
+ */
+#ifndef DAK_B200_H
+#define DAK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DAK_API __attribute__((visibility("default")))
+#else
+#define DAK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+enum dak_status {
+  DAK_OK = 0,
+  DAK_ERR_INVALID_ARG = 1,  /* bad shape, stride, pointer or parameter       */
+  DAK_ERR_UNSUPPORTED = 2,  /* valid but not implemented (dtype, head_dim...) */
+  DAK_ERR_CUDA = 3,         /* a CUDA runtime call failed                     */
+  DAK_ERR_DRIVER = 4,       /* a CUDA driver call failed (tensor-map encode)  */
+  DAK_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up             */
+  DAK_ERR_ALIGNMENT = 6,    /* pointer or stride breaks a 16-byte TMA rule    */
+  DAK_ERR_NO_DEVICE = 7     /* no CUDA device visible                          */
+};
+
+/* Element types (match the dtypes accepted by torch_runtime.cu:87-107). */
+enum dak_dtype {
+  DAK_DTYPE_F16 = 0,
+  DAK_DTYPE_BF16 = 1,
+  DAK_DTYPE_F32 = 2,
+  DAK_DTYPE_U8 = 3,
+  DAK_DTYPE_I32 = 4,
+  DAK_DTYPE_U32 = 5
+};
+
+/* Kernel opcodes, numbered as KERNEL_OPCODES in src/torch_runtime.cu:20-27. */
+enum dak_opcode {
+  DAK_OP_GEMV = 0,
+  DAK_OP_GEMV_HORIZONTAL = 1,
+  DAK_OP_GEMV_MULTICAST = 2,
+  DAK_OP_GEMV_HORIZONTAL_MULTICAST = 3,
+  DAK_OP_GEMV_MULTICAST_PREFILL = 4,
+  DAK_OP_GEMV_HORIZONTAL_MULTICAST_PREFILL = 5
+};
+
+DAK_API const char *dak_strerror(int status);
+/* Detail text of the calling thread's last failing call ("" if none). */
+DAK_API const char *dak_last_error_message(void);
+
+/* ------------------------------------------------------------- constants */
+/* Module attributes NUM_SMS, MAX_COPY_SMS, BUFFER_SLOTS, TILE_N
+ * (src/torch_runtime.cu:440-443; include/task/config.cuh:1-46). */
+typedef struct dak_constants {
+  int num_sms;       /* SMs of the current device (148 on B200)              */
+  int max_copy_sms;  /* CTAs the linear kernels may occupy                    */
+  int buffer_slots;  /* weight pipeline depth of the decode kernel           */
+  int tile_n;        /* largest token count served by the CUDA-core kernel   */
+  int tile_m;        /* output-feature granularity of the split (64)          */
+  int tile_k;        /* K rows per pipeline stage                            */
+  int mma_tile_m;    /* output features per tensor-core tile (128)           */
+  int mma_max_tokens;/* largest token count of one tensor-core launch (256)  */
+  int abi_version;
+} dak_constants;
+DAK_API int dak_get_constants(dak_constants *out);
+
+/* print_device_name (src/runtime.cu:9-16; torch_runtime.cu:419-422). */
+DAK_API int dak_print_device_name(int device_id);
+
+/* set_smem_size (src/torch_runtime.cu:373-417).  The sm_100a kernels size
+ * their own shared memory, so this only validates the opcode and the request
+ * against the device limit; it returns the size in effect, 0 on error. */
+DAK_API size_t dak_set_smem_size(size_t smem_size, int opcode);
+
+/* ------------------------------------------------------------ descriptors */
+/* build_tma_desc (src/torch_runtime.cu:120-191).  Writes a DAK_DESC_BYTES
+ * opaque descriptor of the tensor at `base` (a device pointer or a pinned,
+ * mapped host pointer).  Arguments keep the reference's meaning: shape and
+ * box in elements with the innermost dimension first, strides_bytes of
+ * dimensions 1..rank-1 in bytes, swizzle 0/32/64/128.  The kernels rebuild
+ * their own sm_100a tile maps from it, so the box is only checked. */
+#define DAK_DESC_BYTES 128
+DAK_API int dak_build_tma_desc(void *desc_out, const void *base, int dtype, int rank,
+                       const int64_t *shape, const int64_t *strides_bytes,
+                       const int64_t *box_dim, const int64_t *elem_strides,
+                       int swizzle_bytes);
+
+/* tensormap_replace_address (src/torch_runtime.cu:193-198). */
+DAK_API int dak_tensormap_replace_address(void *desc, const void *new_base);
+
+/* --------------------------------------------------- offloaded linear (a1-a3)
+ * C[N, M] = B[N, K] * A[K, M] in the reference's naming: A is the transposed
+ * weight (out features contiguous), B the activations (N tokens), C the
+ * output.  FP32 accumulation, output written once (no pre-zeroed C needed).
+ * num_copy_blocks / num_copy_host_blocks / *_sms_per_row keep their meaning
+ * (CTAs in total, CTAs reading host rows, CTAs cooperating on one row tile);
+ * 0 in num_copy_blocks selects the automatic B200 schedule.  smem_size is
+ * accepted and ignored. */
+
+/* gemv (src/torch_runtime.cu:201-221; include/task/gemv.cuh:372-405). */
+DAK_API int dak_gemv(const void *a_desc, const void *b_desc, const void *c_desc, int M,
+             int N, int K, int num_copy_blocks, int smem_size, int sms_per_row,
+             void *stream);
+
+/* gemv_horizontal (src/torch_runtime.cu:223-244; gemv.cuh:408-452): output
+ * rows [0, h_M) come from the host-resident A, rows [h_M, h_M+d_M) from the
+ * HBM-resident A. */
+DAK_API int dak_gemv_horizontal(const void *a_desc_h, const void *a_desc_d,
+                        const void *b_desc, const void *c_desc, int h_M,
+                        int d_M, int N, int K, int num_copy_blocks,
+                        int num_copy_host_blocks, int smem_size,
+                        int h_sms_per_row, int d_sms_per_row, void *stream);
+
+/* gemv_multicast / gemv_multicast_prefill (torch_runtime.cu:313-361;
+ * gemv_multicast.cuh:185-376, 869-886).  Same contract as dak_gemv; served by
+ * the tcgen05 kernel, which loads every weight tile once and uses no cluster
+ * multicast. */
+DAK_API int dak_gemv_multicast(const void *a_desc, const void *b_desc,
+                       const void *c_desc, int M, int N, int K,
+                       int num_copy_blocks, int smem_size, int sms_per_row,
+                       void *stream);
+DAK_API int dak_gemv_multicast_prefill(const void *a_desc, const void *b_desc,
+                               const void *c_desc, int M, int N, int K,
+                               int num_copy_blocks, int smem_size,
+                               int sms_per_row, void *stream);
+
+/* gemv_horizontal_multicast(_prefill) (torch_runtime.cu:247-311;
+ * gemv_multicast.cuh:572-597, 889-914).  Same contract as dak_gemv_horizontal. */
+DAK_API int dak_gemv_horizontal_multicast(const void *a_desc_h, const void *a_desc_d,
+                                  const void *b_desc, const void *c_desc,
+                                  int h_M, int d_M, int N, int K,
+                                  int num_copy_blocks, int num_copy_host_blocks,
+                                  int smem_size, int h_sms_per_row,
+                                  int d_sms_per_row, void *stream);
+DAK_API int dak_gemv_horizontal_multicast_prefill(
+    const void *a_desc_h, const void *a_desc_d, const void *b_desc,
+    const void *c_desc, int h_M, int d_M, int N, int K, int num_copy_blocks,
+    int num_copy_host_blocks, int smem_size, int h_sms_per_row,
+    int d_sms_per_row, void *stream);
+
+/* Pointer-level form of the split linear that all the gemv* entry points
+ * reduce to.  The weight is stored transposed, as the reference's
+ * LinearHorizontal keeps it (app/python/layers/linearLayer.py:207-246):
+ * w_host is [K, host_cols] with row stride ld_host elements, w_dev is
+ * [K, dev_cols]; x is [ntok, K]; y is [ntok, *] and receives the host columns
+ * at y[:, host_col_offset:...] and the device columns at y[:, dev_col_offset:...]. */
+enum dak_linear_path {
+  DAK_PATH_AUTO = 0,      /* CUDA-core for few tokens, tensor cores above    */
+  DAK_PATH_CUDA_CORE = 1, /* FP32 FMA + warp-shuffle reduction, ntok <= 8     */
+  DAK_PATH_TCGEN05 = 2    /* tcgen05.mma kind::f16, FP32 accumulators in TMEM */
+};
+typedef struct dak_linear_args {
+  const void *w_host;
+  int64_t host_cols, ld_host, host_col_offset;
+  const void *w_dev;
+  int64_t dev_cols, ld_dev, dev_col_offset;
+  const void *x;
+  int64_t ldx;
+  void *y;
+  int64_t ldy;
+  int64_t ntok, K;
+  int dtype;                  /* DAK_DTYPE_F16 or DAK_DTYPE_BF16          */
+  int host_ctas, dev_ctas;    /* 0 = automatic                              */
+  int host_ksplit, dev_ksplit;/* CTAs per output tile along K; 0 = automatic */
+  int path;                   /* enum dak_linear_path                       */
+} dak_linear_args;
+DAK_API int dak_linear_split(const dak_linear_args *args, void *stream);
+
+/* flush_l2_cache (src/torch_runtime.cu:363-371; include/task/utils.cuh:3-14):
+ * reads n floats of `dummy` past L2 and folds them into *sink. */
+DAK_API int dak_flush_l2_cache(float *dummy, size_t n, float *sink, void *stream);
+
+/* ------------------------------------------------ split-KV decode attention */
+/* `opt_attention._C.decode` (opt_attention/csrc/opt_attention_ext.cpp:164-319).
+ * One query token per sequence.  Rows b < host_size read key_host/value_host
+ * (row b), the rest read key/value (row b - host_size), as
+ * opt_attention_kernel.cuh:331-348 does.  K/V rows are [Hkv, S, D] with the
+ * token stride equal to D.  num_q_heads may be a multiple of num_kv_heads
+ * (GQA); the reference only has num_q_heads == num_kv_heads.  Partial results
+ * of the split-KV pass go to the caller's scratch: partial_o holds
+ * batch*num_q_heads*num_splits*head_dim floats and partial_ml
+ * 2*batch*num_q_heads*num_splits floats, num_splits = ceil(S/split_size). */
+typedef struct dak_attn_decode_args {
+  const void *query;        /* [B, Hq, 1, D]                                */
+  int64_t q_stride_b, q_stride_h;
+  const void *key, *value;  /* device rows [B - host_size, Hkv, S, D]       */
+  int64_t kv_stride_b, kv_stride_h;
+  const void *key_host, *value_host; /* pinned rows [host_size, Hkv, S, D]  */
+  int64_t kvh_stride_b, kvh_stride_h;
+  const float *mask;        /* optional additive [B, 1, 1, S] FP32          */
+  int64_t mask_stride_b;
+  void *out;                /* [B, 1, Hq, D]                                */
+  int64_t o_stride_b, o_stride_h;
+  float *partial_o, *partial_ml;
+  int batch, host_size, num_q_heads, num_kv_heads, head_dim, seq_len;
+  int split_size;           /* tokens per split, multiple of 64            */
+  float scaling;
+  int dtype;                /* DAK_DTYPE_F16 or DAK_DTYPE_BF16             */
+} dak_attn_decode_args;
+DAK_API int dak_attn_decode(const dak_attn_decode_args *args, void *stream);
+
+/* Paged form: KV pages of page_size tokens live in two pools, one in HBM and
+ * one in pinned host memory, both laid out [pages, Hkv, page_size, D].
+ * block_table[b * bt_stride + j] names page j of sequence b: a value v >= 0 is
+ * device page v, v < 0 is host page (-1 - v).  No reference counterpart:
+ * the reference has only the batch-split form above. */
+typedef struct dak_attn_paged_args {
+  const void *query;        /* [B, Hq, D]                                   */
+  int64_t q_stride_b, q_stride_h;
+  const void *k_pool_dev, *v_pool_dev;
+  const void *k_pool_host, *v_pool_host;
+  const int32_t *block_table;
+  int64_t bt_stride;
+  const int32_t *seq_lens;  /* [B] tokens per sequence                       */
+  void *out;                /* [B, Hq, D]                                   */
+  int64_t o_stride_b, o_stride_h;
+  float *partial_o, *partial_ml;
+  int batch, num_q_heads, num_kv_heads, head_dim, page_size, max_seq_len;
+  int split_size;           /* tokens per split, multiple of page_size     */
+  float scaling;
+  int dtype;
+} dak_attn_paged_args;
+DAK_API int dak_attn_decode_paged(const dak_attn_paged_args *args, void *stream);
+
+/* ------------------------------------------------------------ diagnostics */
+/* Reads (and with clear != 0 resets) the device-side error word that kernels
+ * set when a bounded wait times out.  Synchronizes the current device. */
+DAK_API int dak_device_status(int clear, int *status_out);
+
+/* Measurement helper: streams `bytes` of `src` (device or pinned host memory)
+ * through shared memory with TMA bulk copies on `ctas` CTAs, each keeping
+ * `stages` copies of `chunk_bytes` in flight; folds a checksum into *sink. */
+DAK_API int dak_probe_stream_read(const void *src, size_t bytes, int ctas, int stages,
+                          int chunk_bytes, uint32_t *sink, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DAK_B200_H */

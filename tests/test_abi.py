@@ -1,0 +1,129 @@
+"""The C ABI library loads and exports every entry point of include/dak_b200.h;
+host-only entry points (descriptors, constants, argument checks) behave as the
+reference's pybind functions do (src/torch_runtime.cu:120-198, 373-417).
+No compute call is made here."""
+import ctypes
+import re
+
+import pytest
+import torch
+
+from conftest import REPO
+
+
+def header_functions():
+    text = (REPO / "include" / "dak_b200.h").read_text()
+    return sorted(set(re.findall(r"DAK_API\s+[\w\s\*]+?\b(dak_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_header_function():
+    from directaccesskernel_b200 import _lib
+
+    names = header_functions()
+    assert len(names) >= 19
+    for n in names:
+        assert hasattr(_lib.LIB, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_constants():
+    from offload import runtime
+
+    assert runtime.NUM_SMS > 0
+    assert runtime.TILE_N == 8
+    assert runtime.BUFFER_SLOTS >= 2
+    assert runtime.MAX_COPY_SMS == runtime.NUM_SMS
+
+
+def test_strerror_and_status_names():
+    from directaccesskernel_b200 import _lib
+
+    assert _lib.LIB.dak_strerror(0) == b"success"
+    assert _lib.LIB.dak_strerror(5) == b"device wait timed out"
+
+
+def test_build_desc_roundtrip_and_replace_address():
+    from directaccesskernel_b200 import runtime
+
+    w = torch.zeros(256, 192, dtype=torch.float16)
+    d = runtime.build_tma_desc(w, [192, 256], [384], [64, 256], [1, 1], 128)
+    assert d.dtype == torch.uint8 and d.numel() == 128 and not d.is_cuda
+    ptr = int.from_bytes(bytes(d[8:16].tolist()), "little")
+    assert ptr == w.data_ptr()
+    w2 = torch.zeros(256, 192, dtype=torch.float16)
+    runtime.tensormap_replace_address(d, w2)
+    assert int.from_bytes(bytes(d[8:16].tolist()), "little") == w2.data_ptr()
+
+
+@pytest.mark.parametrize("bad,msg", [
+    (dict(strides=[384, 1]), "same length"),
+    (dict(box=[64]), "box_dim"),
+    (dict(swizzle=48), "swizzle"),
+    (dict(shape=[0, 256]), "shape\\[0\\] must be > 0"),
+    (dict(strides=[100]), "multiple of 16"),
+    (dict(box=[300, 256]), "box_dim\\[0\\] must be <= 256"),
+    (dict(box=[128, 256]), "swizzle span"),
+])
+def test_build_desc_errors(bad, msg):
+    from directaccesskernel_b200 import runtime
+
+    w = torch.zeros(256, 192, dtype=torch.float16)
+    args = dict(shape=[192, 256], strides=[384], box=[64, 256], es=[1, 1], swizzle=128)
+    args.update(bad)
+    with pytest.raises(RuntimeError, match=msg):
+        runtime.build_tma_desc(w, args["shape"], args["strides"], args["box"], args["es"], args["swizzle"])
+
+
+def test_build_desc_rejects_dtype_and_empty():
+    from directaccesskernel_b200 import runtime
+
+    with pytest.raises(RuntimeError, match="dtype"):
+        runtime.build_tma_desc(torch.zeros(4, 8, dtype=torch.float64), [8, 4], [64], [8, 4], [1, 1], 0)
+    with pytest.raises(RuntimeError, match="storage"):
+        runtime.build_tma_desc(torch.zeros(0, dtype=torch.float16), [8], [], [8], [1], 0)
+
+
+def test_set_smem_size():
+    from directaccesskernel_b200 import runtime
+
+    assert runtime.set_smem_size(112640, runtime.GEMV_HORIZONTAL) == 112640
+    # Unsupported opcode: the reference prints and returns 0 (torch_runtime.cu:397-400).
+    from directaccesskernel_b200 import _lib
+
+    assert _lib.LIB.dak_set_smem_size(1024, 9) == 0
+
+
+def test_gemv_rejects_bad_descriptors_without_launch():
+    from directaccesskernel_b200 import _lib
+
+    junk = (ctypes.c_uint8 * 128)()
+    st = _lib.LIB.dak_gemv(ctypes.addressof(junk), ctypes.addressof(junk), ctypes.addressof(junk), 64, 1, 64,
+                           0, 0, 1, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG
+    assert b"not a DAK descriptor" in _lib.LIB.dak_last_error_message()
+
+
+def test_gemv_shape_mismatch_is_an_error():
+    from directaccesskernel_b200 import runtime
+    from directaccesskernel_b200.utils import build_tma_wgmma_k, build_tma_wgmma_mn
+
+    w = torch.zeros(256, 192, dtype=torch.float16)
+    x = torch.zeros(2, 256, dtype=torch.float16)
+    y = torch.zeros(2, 192, dtype=torch.float16)
+    _, a = build_tma_wgmma_mn(w, 64, 256)
+    _, b = build_tma_wgmma_k(x, 256, 8)
+    _, c = build_tma_wgmma_mn(y, 64, 8)
+    with pytest.raises(RuntimeError, match="expected"):
+        runtime.gemv(a, b, c, 192, 2, 512, 0, 0, 1)  # K does not match A
+
+
+def test_linear_split_argument_checks():
+    from directaccesskernel_b200 import runtime
+
+    x = torch.zeros(2, 64, dtype=torch.float16)
+    y = torch.zeros(2, 64, dtype=torch.float16)
+    with pytest.raises(RuntimeError):
+        runtime.linear_split(x, y, None, torch.zeros(32, 64, dtype=torch.float16))  # K mismatch
+    with pytest.raises(RuntimeError):
+        runtime.linear_split(x, y, None, torch.zeros(64, 64, dtype=torch.float32))  # dtype mismatch
