@@ -149,7 +149,8 @@ __device__ __forceinline__ void record_error(const WaitCtx &w, int code) {
 }
 
 template <bool kClusterScope>
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx &w) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx &w,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
   auto probe = [&]() {
     return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
   };
@@ -161,7 +162,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     if (probe()) return true;
     if ((++n & 15u) == 0) {
       if (*w.abort) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (globaltimer() - t0 > timeout_ns) {
         record_error(w, DAK_ERR_TIMEOUT);
         return false;
       }

@@ -109,6 +109,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 32 lanes x 16 consecutive 32-bit columns (the N = 16 tile).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <int CH>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, float (&v)[CH]) {
+  if constexpr (CH == 32) tmem_ld32(taddr, v);
+  else tmem_ld16(taddr, v);
+}
 
 // Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -289,6 +308,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const int qd = warp & 3;                 // TMEM lane quadrant of this warp
     const int f = qd * 32 + lane;            // feature within the 128-feature tile
     const int owner = (qd * 32) / feat_per_owner;  // rank of the group that writes f
+    // Accumulator columns moved per tcgen05.ld; never more than the tile has.
+    constexpr int kChunkCols = NTOKP < 32 ? NTOKP : 32;
     const uint32_t my_rank = cluster_ctarank();
     const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
     int n = 0;
@@ -308,14 +329,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           if (ks > 1) mbar_wait<true>(red_full, (uint32_t)(nred & 1), wc);
           const int fl = f - owner * feat_per_owner;
 #pragma unroll 1
-          for (int c0 = 0; c0 < NTOKP; c0 += 32) {
-            float v[32];
-            tmem_ld32(acc_addr + (uint32_t)c0, v);
+          for (int c0 = 0; c0 < NTOKP; c0 += kChunkCols) {
+            float v[kChunkCols];
+            tmem_ld_chunk<kChunkCols>(acc_addr + (uint32_t)c0, v);
             if (ks > 1) {
               for (int m = 0; m < ks - 1; ++m) {
                 const float *src = red + ((size_t)m * feat_per_owner + fl) * L.red_row + c0;
 #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
+                for (int j = 0; j < kChunkCols; j += 4) {
                   const float4 a = *reinterpret_cast<const float4 *>(src + j);
                   v[j] += a.x; v[j + 1] += a.y; v[j + 2] += a.z; v[j + 3] += a.w;
                 }
@@ -323,7 +344,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             }
             if (col_ok) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
+              for (int j = 0; j < kChunkCols; ++j)
                 if (c0 + j < p.ntok)
                   reinterpret_cast<uint16_t *>(ycol)[(long long)(c0 + j) * p.ldy] =
                       Elem<T>::from_float(v[j]);
@@ -344,11 +365,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           const uint32_t dst_base = mapa_shared(
               smem_u32(red + ((size_t)slot * feat_per_owner + fl) * L.red_row), owner_rank);
 #pragma unroll 1
-          for (int c0 = 0; c0 < NTOKP; c0 += 32) {
-            float v[32];
-            tmem_ld32(acc_addr + (uint32_t)c0, v);
+          for (int c0 = 0; c0 < NTOKP; c0 += kChunkCols) {
+            float v[kChunkCols];
+            tmem_ld_chunk<kChunkCols>(acc_addr + (uint32_t)c0, v);
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
+            for (int j = 0; j < kChunkCols; j += 4)
               st_cluster_v4(dst_base + (uint32_t)(c0 + j) * 4, v[j], v[j + 1], v[j + 2], v[j + 3]);
           }
           mbar_arrive_remote(mapa_shared(red_full, owner_rank));

@@ -575,6 +575,21 @@ __global__ void probe_read_kernel(const uint8_t *src, size_t bytes, int stages, 
     atomicXor(sink, x);
   }
 }
+// A wait that nothing completes: gives up after timeout_ns, leaving
+// DAK_ERR_TIMEOUT in the status word (the path every kernel takes when a copy
+// or a peer never arrives).
+__global__ void selftest_wait_kernel(int *status, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const WaitCtx wc{&abort_flag, status};
+  mbar_wait<false>(smem_u32(&bar), 0, wc, timeout_ns);
+}
 }  // namespace
 
 }  // namespace dak
@@ -780,6 +795,17 @@ int dak_device_status(int clear, int *status_out) {
   }
   if (status_out) *status_out = v;
   return DAK_OK;
+}
+
+int dak_selftest_wait_timeout(unsigned int timeout_us, void *stream) {
+  if (timeout_us == 0 || timeout_us > 10000000u)
+    return fail(DAK_ERR_INVALID_ARG, "timeout_us must be in (0, 10 s]");
+  DeviceInfo *dev;
+  int st = device_info(&dev);
+  if (st) return st;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev->status,
+                                                                        (unsigned long long)timeout_us * 1000ull);
+  return cuda_status(cudaGetLastError(), "selftest launch");
 }
 
 int dak_probe_stream_read(const void *src, size_t bytes, int ctas, int stages, int chunk_bytes,

@@ -1,0 +1,110 @@
+"""Tensor-parallel offloaded linear layers for one 8xB200 box.
+
+The reference has no multi-GPU code.  These layers shard a linear layer
+Megatron-style over a torch.distributed process group (NCCL over NVLink on the
+GPUs, gloo in the CPU tests):
+  * ColumnParallelLinear: rank r owns output features [r*N/G, (r+1)*N/G); the
+    local result is all-gathered when ``gather_output`` (q/k/v, gate/up and
+    lm_head keep it sharded);
+  * RowParallelLinear: rank r owns input features [r*K/G, (r+1)*K/G) and
+    consumes the matching slice of its input; the partial products are summed
+    with one all-reduce (o and down projections).
+Each rank's shard is an ordinary offloaded module (LinearHorizontal and
+friends), split between that GPU's HBM and pinned host memory on the GPU's own
+NUMA node, so every GPU streams its own host rows over its own host link.  The
+collectives run on the current stream after the local kernel.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+
+def shard_rows(weight: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Output-feature shard [N/G, K] of an nn.Linear weight [N, K]."""
+    n = weight.shape[0]
+    if n % world:
+        raise ValueError(f"out_features {n} is not divisible by the tensor-parallel size {world}")
+    step = n // world
+    return weight[rank * step:(rank + 1) * step]
+
+
+def shard_cols(weight: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Input-feature shard [N, K/G] of an nn.Linear weight [N, K]."""
+    k = weight.shape[1]
+    if k % world:
+        raise ValueError(f"in_features {k} is not divisible by the tensor-parallel size {world}")
+    step = k // world
+    return weight[:, rank * step:(rank + 1) * step]
+
+
+def _group_info(group):
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+class ColumnParallelLinear(nn.Module):
+    """y = x W^T with W's rows sharded; ``local`` computes x W_r^T for this rank."""
+
+    def __init__(self, local: nn.Module, out_features: int, group=None, gather_output: bool = True):
+        super().__init__()
+        self.local = local
+        self.group = group
+        self.out_features = out_features
+        self.gather_output = gather_output
+        self.rank, self.world = _group_info(group)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        y = self.local(x)
+        if not self.gather_output or self.world == 1:
+            return y
+        y2 = y.reshape(-1, y.shape[-1]).contiguous()
+        parts = torch.empty((self.world * y2.shape[0], y2.shape[1]), dtype=y.dtype, device=y.device)
+        dist.all_gather_into_tensor(parts, y2, group=self.group)
+        # [G * rows, N/G] -> [rows, N]: shard r holds output features r*N/G .. (r+1)*N/G.
+        full = parts.view(self.world, y2.shape[0], y2.shape[1]).permute(1, 0, 2).reshape(y2.shape[0], -1)
+        return full.reshape(*y.shape[:-1], self.out_features)
+
+
+class RowParallelLinear(nn.Module):
+    """y = x W^T with W's columns sharded; partial products summed by all-reduce."""
+
+    def __init__(self, local: nn.Module, in_features: int, group=None, input_is_parallel: bool = False):
+        super().__init__()
+        self.local = local
+        self.group = group
+        self.in_features = in_features
+        self.input_is_parallel = input_is_parallel
+        self.rank, self.world = _group_info(group)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not self.input_is_parallel and self.world > 1:
+            step = self.in_features // self.world
+            x = x[..., self.rank * step:(self.rank + 1) * step].contiguous()
+        y = self.local(x)
+        if self.world > 1:
+            dist.all_reduce(y, group=self.group)
+        return y
+
+
+def make_offloaded_shard(weight_shard: torch.Tensor, offload_ratio: float, *, host_side: str = "first",
+                         device: str | torch.device = "cuda") -> nn.Module:
+    """An offloaded module holding ``weight_shard`` ([N_r, K_r]): LinearHorizontal
+    for 0 < r < 1, a single-tier Linear in HBM (r = 0) or pinned host memory (r = 1)."""
+    from .layers import Linear, LinearHorizontal
+    from .utils import get_smem_size
+
+    n, k = weight_shard.shape
+    dt = weight_shard.dtype if weight_shard.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    if 0.0 < offload_ratio < 1.0:
+        mod = LinearHorizontal(k, n, get_smem_size(), 0, device=device, dtype=dt, skip_init=True)
+        with torch.no_grad():
+            mod.weight.copy_(weight_shard)
+        mod.horizontal_split_weight(offload_ratio, 0, 0, 1, 1, host_side=host_side)
+    else:
+        mod = Linear(k, n, get_smem_size(), 0, device=device, dtype=dt, skip_init=True)
+        with torch.no_grad():
+            mod.weight.copy_(weight_shard)
+        mod.move_weight_to_device("cpu" if offload_ratio >= 1.0 else "cuda")
+    mod.build_tma_desc()
+    return mod

@@ -248,6 +248,13 @@ DAK_API int dak_attn_decode_paged(const dak_attn_paged_args *args, void *stream)
  * set when a bounded wait times out.  Synchronizes the current device. */
 DAK_API int dak_device_status(int clear, int *status_out);
 
+/* Failure-path self test (no reference counterpart): launches one CTA whose
+ * mbarrier wait can never complete; the wait gives up after timeout_us
+ * microseconds, records DAK_ERR_TIMEOUT in the device error word and the
+ * kernel exits, leaving the context usable.  This is the path every kernel
+ * takes when a copy or a peer never arrives. */
+DAK_API int dak_selftest_wait_timeout(unsigned int timeout_us, void *stream);
+
 /* Measurement helper: streams `bytes` of `src` (device or pinned host memory)
  * through shared memory with TMA bulk copies on `ctas` CTAs, each keeping
  * `stages` copies of `chunk_bytes` in flight; folds a checksum into *sink. */
