@@ -108,6 +108,7 @@ SIGNATURES = {
     "dak_flush_l2_cache": (c_int, [c_vp, ctypes.c_size_t, c_vp, c_vp]),
     "dak_attn_decode": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_attn_decode_paged": (c_int, [ctypes.POINTER(AttnPagedArgs), c_vp]),
+    "dak_attn_decode_noalloc": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_device_status": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "dak_selftest_wait_timeout": (c_int, [ctypes.c_uint, c_vp]),
     "dak_probe_stream_read": (c_int, [c_vp, ctypes.c_size_t, c_int, c_int, c_int, c_vp, c_vp]),

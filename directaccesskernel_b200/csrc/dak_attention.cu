@@ -585,3 +585,61 @@ int dak_attn_decode_paged(const dak_attn_paged_args *a, void *stream) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------- allocation-free variant
+// dak_attn_decode needs the caller to pass FP32 scratch for the per-split
+// partial results.  Some callers have no way to allocate it: a host that binds
+// only this C ABI and owns no device allocator, or an engine that reserves all
+// free device memory at start-up so that any later cudaMalloc fails (and
+// cudaMalloc/cudaFree may synchronize the device, which a decode loop cannot
+// afford).  dak_attn_decode_noalloc serves them with scratch that lives in the
+// library itself: a fixed array in device global memory, present on every GPU
+// that loads the library, for the life of the process.
+namespace dak {
+namespace {
+constexpr size_t kNoAllocScratchFloats = size_t(2) << 20;  // 8 MiB
+static __device__ __align__(256) float g_attn_noalloc_scratch[kNoAllocScratchFloats];
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float *g_noalloc_ptr[kNoAllocMaxDevices];
+}  // namespace
+}  // namespace dak
+
+extern "C" int dak_attn_decode_noalloc(const dak_attn_decode_args *args, void *stream) {
+  using namespace dak;
+  if (!args) return fail(DAK_ERR_INVALID_ARG, "args is null");
+  if (args->split_size <= 0 || args->seq_len <= 0 || args->batch <= 0 || args->num_q_heads <= 0 ||
+      args->head_dim <= 0)
+    return fail(DAK_ERR_INVALID_ARG, "batch, heads, head_dim, seq_len and split_size must be positive");
+  const size_t splits = ((size_t)args->seq_len + args->split_size - 1) / args->split_size;
+  const size_t rows = (size_t)args->batch * (size_t)args->num_q_heads * splits;
+  const size_t need = rows * ((size_t)args->head_dim + 2);
+  if (need > kNoAllocScratchFloats)
+    return fail(DAK_ERR_INVALID_ARG,
+                "dak_attn_decode_noalloc: batch x q_heads x splits x (head_dim + 2) = %zu floats exceeds "
+                "its built-in scratch of %zu floats (8 MiB); raise split_size or use dak_attn_decode",
+                need, kNoAllocScratchFloats);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(DAK_ERR_UNSUPPORTED, "device %d out of range", dev);
+  float *scratch;
+  {
+    // First call on this device: look up where the array lives on it.  In host
+    // code the array's name is only a stand-in, never a device address.
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void *ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_attn_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(scratch)");
+      g_noalloc_ptr[dev] = static_cast<float *>(ptr);
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  // Every partial (o, m, l) the merge reads is written earlier in the same
+  // call, so the array needs no clearing between calls.
+  dak_attn_decode_args a = *args;
+  a.partial_o = scratch;
+  a.partial_ml = scratch + rows * (size_t)args->head_dim;
+  return dak_attn_decode(&a, stream);
+}

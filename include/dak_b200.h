@@ -220,6 +220,24 @@ typedef struct dak_attn_decode_args {
 } dak_attn_decode_args;
 DAK_API int dak_attn_decode(const dak_attn_decode_args *args, void *stream);
 
+/* Allocation-free form of dak_attn_decode, with no counterpart in the
+ * reference.  For callers that cannot allocate device memory: a host that binds
+ * only this C ABI and has no device allocator of its own, or an engine that
+ * has reserved all free device memory up front, so cudaMalloc would fail (and
+ * cudaMalloc/cudaFree may synchronize the device).  The caller passes inputs
+ * and outputs as for dak_attn_decode; args->partial_o and args->partial_ml are
+ * ignored.  The split-KV partials go to an 8 MiB array inside the library,
+ * held on every GPU that loads it until the process exits, so
+ * batch * num_q_heads * ceil(seq_len / split_size) * (head_dim + 2) must not
+ * exceed 2,097,152 floats; larger calls fail with DAK_ERR_INVALID_ARG.  The
+ * first call on a device looks up the array's address there, so make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls that can overlap on the GPU (different streams, different threads)
+ * race on it and must be serialized by the caller.  The array keeps the last
+ * call's contents; each call writes every partial it reads, so nothing needs
+ * clearing.  Allocates nothing. */
+DAK_API int dak_attn_decode_noalloc(const dak_attn_decode_args *args, void *stream);
+
 /* Paged form: KV pages of page_size tokens live in two pools, one in HBM and
  * one in pinned host memory, both laid out [pages, Hkv, page_size, D].
  * block_table[b * bt_stride + j] names page j of sequence b: a value v >= 0 is
