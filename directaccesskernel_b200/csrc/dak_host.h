@@ -21,15 +21,54 @@ int *device_status_word();
 int check_gpu_accessible(const void *p, const char *what);
 
 // Shared-memory bytes and launch of the CUDA-core kernel for `ntok_tmpl`
-// (1, 2, 4 or 8) tokens and dtype (DAK_DTYPE_F16 / _BF16).
+// (1, 2, 4 or 8) tokens and dtype (DAK_DTYPE_F16 / _BF16).  With grid == 0
+// nothing is launched and *max_clusters (if given) receives how many
+// clusters of `cluster` CTAs can be resident at once.
 size_t linear_core_smem_bytes(int ntok_tmpl, int red_slots);
+int linear_core_stages(int ntok_tmpl, int red_slots);
 cudaError_t launch_linear_core(const LinearParams &p, int ntok_tmpl, int dtype, int grid,
-                               int cluster, size_t smem, cudaStream_t stream);
+                               int cluster, size_t smem, cudaStream_t stream,
+                               int *max_clusters = nullptr);
 
 // Same for the tcgen05 kernel; `ntok_tmpl` is the UMMA N (multiple of 16).
 size_t linear_mma_smem_bytes(int ntok_tmpl, int red_slots);
 int linear_mma_stages(int ntok_tmpl, int ksplit);
 cudaError_t launch_linear_mma(const LinearParams &p, int ntok_tmpl, int dtype, int grid,
-                              int cluster, size_t smem, cudaStream_t stream);
+                              int cluster, size_t smem, cudaStream_t stream,
+                              int *max_clusters = nullptr);
+
+// Launch (or, with grid == 0, occupancy query) of a linear kernel: 1-D grid,
+// 1-D clusters, programmatic stream serialization when p.pdl is set.
+template <typename Kern>
+cudaError_t launch_linear_kernel(Kern kern, const LinearParams &p, int grid, int threads, int cluster,
+                                 size_t smem, cudaStream_t stream, int *max_clusters) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  if (cluster > 8) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid > 0 ? grid : cluster);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (grid <= 0) {
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (max_clusters) *max_clusters = n;
+    return e;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
 
 }  // namespace dak

@@ -16,17 +16,20 @@ namespace dak {
 constexpr int kBoxCols = 64;  // 64 x 16-bit = 128 B = one 128-byte swizzle span
 
 // ---- CUDA-core decode kernel (ntok <= 8) ---------------------------------
-constexpr int kCoreBN = 256;                      // output features per tile
-constexpr int kCoreBoxes = kCoreBN / kBoxCols;    // 4 TMA boxes per stage
-constexpr int kCoreBK = 32;                       // K rows per stage
-constexpr int kCoreStages = 8;                    // 8 x 16 KB weight stages
+// Stage shapes follow a measured rule of this part: TMA streams a [K, N]
+// weight at 6.4-6.5 TB/s with boxes of 64 x 64 (8 KB) and four adjacent boxes
+// per row (512 contiguous bytes), but at 3.5 TB/s with 64 x 32 boxes.
+constexpr int kCoreBN = 256;                      // output features per tile (4 boxes)
+constexpr int kCoreBoxes = kCoreBN / kBoxCols;    // TMA boxes per stage
+constexpr int kCoreBK = 64;                       // K rows per stage (8 KB boxes)
+constexpr int kCoreStages = 6;                    // most weight stages (32 KB each)
 constexpr int kCoreConsumerWarps = 8;
 constexpr int kCoreThreads = (kCoreConsumerWarps + 1) * 32;
 constexpr int kCoreMaxTok = 8;
 
 // ---- tcgen05 kernel (ntok up to 256) --------------------------------------
-constexpr int kMmaBM = 128;                       // UMMA M: output features per tile
-constexpr int kMmaBK = 64;                        // K rows per stage (4 x UMMA K=16)
+constexpr int kMmaBM = 128;                       // UMMA M: output features per tile (2 boxes)
+constexpr int kMmaBK = 128;                       // K rows per stage (8 x UMMA K=16; 16 KB boxes)
 constexpr int kMmaMaxTok = 256;                   // UMMA N limit
 constexpr int kMmaEpiWarps = 4;
 constexpr int kMmaThreads = (2 + kMmaEpiWarps) * 32;  // producer, MMA, 4 epilogue
@@ -41,6 +44,20 @@ struct alignas(64) LinearTier {
   int pad_[3];
 };
 
+// Work of group g (ksplit consecutive CTAs) of a tier with `groups` groups:
+// the contiguous 64-feature boxes [box_begin, box_end), split evenly so that
+// no group gets more than one box above the average, walked as tiles of up to
+// `boxes_per_tile` boxes; every CTA of the group covers its own K range.
+struct GroupWork {
+  int box_begin, box_end, ntiles;
+  __host__ __device__ GroupWork(int cols, int groups, int g, int boxes_per_tile) {
+    const int boxes = (cols + kBoxCols - 1) / kBoxCols;
+    box_begin = (int)((long long)g * boxes / groups);
+    box_end = (int)((long long)(g + 1) * boxes / groups);
+    ntiles = (box_end - box_begin + boxes_per_tile - 1) / boxes_per_tile;
+  }
+};
+
 struct alignas(64) LinearParams {
   LinearTier tier[2];  // [0] host tier, [1] device tier
   CUtensorMap xmap;    // x[ntok, K] activations
@@ -51,7 +68,9 @@ struct alignas(64) LinearParams {
   int *status;         // device error word
   int red_slots;       // partial-sum slots reserved in shared memory (max ksplit - 1)
   int stages;          // pipeline depth (tcgen05 kernel; sized to the shared memory left)
-  int pad_[2];
+  int pdl;             // launched with programmatic stream serialization: weights are
+                       // prefetched before griddepcontrol.wait, x and y only after it
+  int pad_[1];
 };
 
 }  // namespace dak

@@ -10,14 +10,17 @@
 // dimension (16..256), so one CTA applies each weight tile to all tokens and no
 // weight byte is fetched twice - no multicast is needed or used.
 //
-// Roles (192 threads): warp 0 issues TMA loads (two 64x64 weight boxes with
-// 128-byte swizzle, MN-major, plus the 64-wide activation slice, K-major, per
-// stage); warp 1 owns TMEM and issues the MMAs from one lane; warps 2..5 read
-// the accumulators back with tcgen05.ld (each warp its TMEM lane quadrant) and
-// write the 16-bit output.  Tiles split along K over `ksplit` CTAs of a cluster
-// are reduce-scattered through DSMEM: each CTA of the group owns 128/ksplit
-// features of the tile, receives the other CTAs' partials for them in its own
-// shared memory and writes them out.
+// Roles (192 threads): warp 0 issues TMA loads (two 64-feature x 128-row
+// weight boxes with 128-byte swizzle, MN-major, plus two 64-wide activation
+// boxes, K-major, per stage); warp 1 owns TMEM and issues the MMAs from one
+// lane; warps 2..5 read the accumulators back with tcgen05.ld (each warp its
+// TMEM lane quadrant) and write the 16-bit output.  Each group of `ksplit`
+// CTAs owns a contiguous, evenly sized range of 64-feature boxes, walked as
+// 128-feature tiles; the CTAs of a group split K and reduce-scatter through
+// DSMEM: each owns 128/ksplit features of the tile, receives the other CTAs'
+// partials for them in its own shared memory and writes them out.  Launched
+// with programmatic stream serialization, the producer fills the ring with
+// weights before waiting for the previous kernel of the stream.
 #include "dak_common.cuh"
 #include "dak_host.h"
 #include "dak_linear.cuh"
@@ -28,8 +31,9 @@ namespace dak {
 
 namespace {
 
-constexpr uint32_t kMmaBoxBytes = kBoxCols * kMmaBK * 2;       // 8 KB (64 x 64)
-constexpr uint32_t kMmaWStageBytes = 2 * kMmaBoxBytes;         // 16 KB (128 x 64)
+constexpr uint32_t kMmaBoxBytes = kBoxCols * kMmaBK * 2;       // 16 KB (64 x 128)
+constexpr uint32_t kMmaWStageBytes = 2 * kMmaBoxBytes;         // 32 KB (128 x 128)
+constexpr int kMmaBoxesPerTile = kMmaBM / kBoxCols;            // 2
 constexpr int kMmaMaxKsplit = 4;
 constexpr int kMmaMaxStages = 8;
 constexpr uint32_t kSmemPerBlock = 227 * 1024;
@@ -38,7 +42,9 @@ constexpr uint32_t kSmemPerBlock = 227 * 1024;
 // stages and the split-K receive buffer fit in one SM's shared memory.
 template <int NTOKP>
 struct MmaLayout {
-  static constexpr uint32_t x_stage_bytes = NTOKP * 128;  // NTOKP rows x 64 k x 2 B
+  // Activations: two K-major 128-byte-swizzled boxes of NTOKP rows x 64 k.
+  static constexpr uint32_t x_box_bytes = NTOKP * 128;
+  static constexpr uint32_t x_stage_bytes = 2 * x_box_bytes;
   static constexpr uint32_t red_row = NTOKP + 4;  // floats per feature row (padded)
   int stages;
   uint32_t w_off, x_off, bar_off, misc_off, red_off;
@@ -175,7 +181,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int r = local - g * ks;
   // CTAs that only pad the tier to a whole number of clusters do no work.
   const bool idle = local >= tier.cta_count;
-  const int ntiles = (tier.cols + kMmaBM - 1) / kMmaBM;
+  const GroupWork work(tier.cols, groups > 0 ? groups : 1, g, kMmaBoxesPerTile);
+  const int ntiles = idle ? 0 : work.ntiles;
+  auto tile_box0 = [&](int j) { return work.box_begin + j * kMmaBoxesPerTile; };
+  auto tile_nbox = [&](int j) { return min(kMmaBoxesPerTile, work.box_end - tile_box0(j)); };
   const int nkb = (p.K + kMmaBK - 1) / kMmaBK;
   const int kb0 = (int)((long long)r * nkb / ks);
   const int kb1 = (int)((long long)(r + 1) * nkb / ks);
@@ -219,6 +228,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  // The next layer may be scheduled now: it only prefetches its own weights
+  // until this grid has completed.
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -227,31 +239,41 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       prefetch_tensormap(&p.xmap);
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      int s = 0;
-      uint32_t ph = 0, issued_mask = 0, issued_par = 0;
-      bool aborted = false;
-      for (int tile = idle ? ntiles : g; tile < ntiles && !aborted; tile += groups) {
-        const int nbox = min(2, (tier.cols - tile * kMmaBM + kBoxCols - 1) / kBoxCols);
-        const uint32_t bytes = (uint32_t)nbox * kMmaBoxBytes + L.x_stage_bytes;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait<false>(empty0 + 8 * s, ph ^ 1u, wc)) {
-            aborted = true;
-            break;
-          }
-          const uint32_t fb = full0 + 8 * s;
-          mbar_arrive_expect_tx(fb, bytes);
-          const uint32_t wdst = sbase + L.w_off + s * kMmaWStageBytes;
-          for (int bx = 0; bx < nbox; ++bx)
-            tma_load_2d(wdst + bx * kMmaBoxBytes, &tier.wmap, tile * kMmaBM + bx * kBoxCols,
-                        kb * kMmaBK, fb, pol_w);
-          tma_load_2d(sbase + L.x_off + s * L.x_stage_bytes, &p.xmap, kb * kMmaBK, 0, fb, pol_x);
-          issued_mask |= 1u << s;
-          issued_par = (issued_par & ~(1u << s)) | (ph << s);
-          if (++s == S) {
-            s = 0;
-            ph ^= 1u;
-          }
-        }
+      uint32_t issued_mask = 0, issued_par = 0;
+      // Work items in order: tiles g, g+groups, ... each over k blocks [kb0, kb1).
+      const int nk = kb1 - kb0;
+      const int total = ntiles * nk;
+      auto w_loads = [&](int i, uint32_t fb) {
+        const int j = i / nk, kb = kb0 + i % nk;
+        const int nbox = tile_nbox(j);
+        mbar_arrive_expect_tx(fb, (uint32_t)nbox * kMmaBoxBytes + L.x_stage_bytes);
+        const uint32_t wdst = sbase + L.w_off + (i % S) * kMmaWStageBytes;
+        for (int bx = 0; bx < nbox; ++bx)
+          tma_load_2d(wdst + bx * kMmaBoxBytes, &tier.wmap, (tile_box0(j) + bx) * kBoxCols, kb * kMmaBK, fb, pol_w);
+      };
+      auto x_load = [&](int i, uint32_t fb) {
+        const uint32_t xdst = sbase + L.x_off + (i % S) * L.x_stage_bytes;
+        for (int h = 0; h < 2; ++h)
+          tma_load_2d(xdst + h * L.x_box_bytes, &p.xmap, (kb0 + i % nk) * kMmaBK + h * 64, 0, fb, pol_x);
+      };
+      // Weights do not depend on the previous kernel of the stream: fill the
+      // ring with them first, then wait for that kernel before touching x.
+      const int pre = p.pdl ? min(total, S) : 0;
+      for (int i = 0; i < pre; ++i) w_loads(i, full0 + 8 * i);
+      griddep_wait();
+      for (int i = 0; i < pre; ++i) {
+        x_load(i, full0 + 8 * i);
+        issued_mask |= 1u << i;
+      }
+      for (int i = pre; i < total; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (uint32_t)((i / S) & 1);
+        if (!mbar_wait<false>(empty0 + 8 * s, ph ^ 1u, wc)) break;
+        const uint32_t fb = full0 + 8 * s;
+        w_loads(i, fb);
+        x_load(i, fb);
+        issued_mask |= 1u << s;
+        issued_par = (issued_par & ~(1u << s)) | (ph << s);
       }
       if (*abort_flag) {
         const WaitCtx drain{reinterpret_cast<volatile int *>(smem + L.misc_off + 8), p.status};
@@ -268,7 +290,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       int n = 0;
-      for (int tile = idle ? ntiles : g; tile < ntiles; tile += groups, ++n) {
+      for (int j = 0; j < ntiles; ++j, ++n) {
         const int ab = n & 1;
         const uint32_t use = (uint32_t)(n >> 1);
         // Wait until the epilogue drained this accumulator buffer.
@@ -286,8 +308,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               for (int kk = 0; kk < kMmaBK / 16; ++kk) {
                 // A: MN-major SW128; 16 K rows = 2 KB; LBO = next 64-feature box, SBO = 8 rows.
                 const uint64_t ad = smem_desc_sw128(wst + kk * 2048, kMmaBoxBytes, 1024);
-                // B: K-major SW128; 16 K elements = 32 B inside the swizzle span; SBO = 8 rows.
-                const uint64_t bd = smem_desc_sw128(xst + kk * 32, 16, 1024);
+                // B: K-major SW128; 64 K per box, 16 K = 32 B inside the swizzle span; SBO = 8 rows.
+                const uint64_t bd = smem_desc_sw128(xst + (kk >> 2) * L.x_box_bytes + (kk & 3) * 32, 16, 1024);
                 tc_mma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
               }
             }
@@ -305,6 +327,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- epilogue
+    griddep_wait();  // y may still be read by the previous kernel of the stream
     const int qd = warp & 3;                 // TMEM lane quadrant of this warp
     const int f = qd * 32 + lane;            // feature within the 128-feature tile
     const int owner = (qd * 32) / feat_per_owner;  // rank of the group that writes f
@@ -315,14 +338,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     int n = 0;
     int nred = 0;
     if (kb1 > kb0) {
-      for (int tile = idle ? ntiles : g; tile < ntiles; tile += groups, ++n) {
+      for (int j = 0; j < ntiles; ++j, ++n) {
         const int ab = n & 1;
         const uint32_t use = (uint32_t)(n >> 1);
         mbar_wait<false>(tfull0 + 8 * ab, use & 1u, wc);
         tc_fence_after();
         const uint32_t acc_addr = tmem_base + lane_addr + (uint32_t)(ab * NTOKP);
-        const int col = tile * kMmaBM + f;
-        const bool col_ok = col < tier.cols;
+        const int col = tile_box0(j) * kBoxCols + f;
+        const bool col_ok = f < tile_nbox(j) * kBoxCols && col < tier.cols;
         T *ycol = reinterpret_cast<T *>(p.y) + tier.col_offset + col;
 
         if (ks == 1 || owner == r) {
@@ -388,36 +411,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, L.tmem_cols());
 }
 
-template <typename T, int NTOKP>
-cudaError_t launch_typed(const LinearParams &p, int grid, int cluster, size_t smem,
-                         cudaStream_t stream) {
-  auto kern = linear_mma_kernel<T, NTOKP>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kMmaThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p);
-}
-
 template <typename T>
 cudaError_t launch_dtype(const LinearParams &p, int ntokp, int grid, int cluster, size_t smem,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, int *mc) {
   switch (ntokp) {
-    case 16: return launch_typed<T, 16>(p, grid, cluster, smem, stream);
-    case 32: return launch_typed<T, 32>(p, grid, cluster, smem, stream);
-    case 64: return launch_typed<T, 64>(p, grid, cluster, smem, stream);
-    case 128: return launch_typed<T, 128>(p, grid, cluster, smem, stream);
-    case 256: return launch_typed<T, 256>(p, grid, cluster, smem, stream);
+    case 16: return launch_linear_kernel(linear_mma_kernel<T, 16>, p, grid, kMmaThreads, cluster, smem, stream, mc);
+    case 32: return launch_linear_kernel(linear_mma_kernel<T, 32>, p, grid, kMmaThreads, cluster, smem, stream, mc);
+    case 64: return launch_linear_kernel(linear_mma_kernel<T, 64>, p, grid, kMmaThreads, cluster, smem, stream, mc);
+    case 128: return launch_linear_kernel(linear_mma_kernel<T, 128>, p, grid, kMmaThreads, cluster, smem, stream, mc);
+    case 256: return launch_linear_kernel(linear_mma_kernel<T, 256>, p, grid, kMmaThreads, cluster, smem, stream, mc);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -462,10 +464,10 @@ size_t linear_mma_smem_bytes(int ntokp, int red_slots) {
 }
 
 cudaError_t launch_linear_mma(const LinearParams &p, int ntokp, int dtype, int grid, int cluster,
-                              size_t smem, cudaStream_t stream) {
-  if (dtype == DAK_DTYPE_F16) return launch_dtype<__half>(p, ntokp, grid, cluster, smem, stream);
+                              size_t smem, cudaStream_t stream, int *max_clusters) {
+  if (dtype == DAK_DTYPE_F16) return launch_dtype<__half>(p, ntokp, grid, cluster, smem, stream, max_clusters);
   if (dtype == DAK_DTYPE_BF16)
-    return launch_dtype<__nv_bfloat16>(p, ntokp, grid, cluster, smem, stream);
+    return launch_dtype<__nv_bfloat16>(p, ntokp, grid, cluster, smem, stream, max_clusters);
   return cudaErrorInvalidValue;
 }
 

@@ -286,7 +286,7 @@ int desc_to_matrix(const void *blob, const char *what, MatView *out) {
 
 // ---------------------------------------------------------- the split linear
 namespace {
-constexpr int kAutoHostCtas = 16;
+constexpr int kAutoHostCtas = 8;  // two CTAs with 4 x 32 KB in flight already saturate PCIe Gen5
 constexpr int kCoreMaxKsplit = 8;
 constexpr int kMmaMaxKsplitHost = 4;
 
@@ -326,6 +326,52 @@ TierPlan user_plan(int ctas, int spr, int tiles, int nkb, int max_ks) {
   t.ksplit = ks;
   t.ctas = std::max(ks, (ctas / ks) * ks);
   return t;
+}
+
+// DAK_B200_TRACE_PLAN=1 prints every launch plan of the linear kernels to stderr.
+bool trace_plans() {
+  static const bool on = [] {
+    const char *v = getenv("DAK_B200_TRACE_PLAN");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
+}
+
+// Programmatic dependent launch of the linear kernels; DAK_B200_NO_PDL=1 turns it off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("DAK_B200_NO_PDL");
+    return !(v && v[0] && v[0] != '0');
+  }();
+  return on;
+}
+
+// CTAs of one launch that can be resident at once, for a kernel variant and
+// cluster size (cached occupancy query).
+int max_resident_ctas(bool mma, int tmpl, int dtype, int cluster, size_t smem, int num_sms) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t key = ((uint64_t)dev << 56) | ((uint64_t)mma << 55) | ((uint64_t)(dtype & 7) << 52) |
+                       ((uint64_t)(tmpl & 0x3FF) << 40) | ((uint64_t)(cluster & 0xFF) << 32) | (uint64_t)smem;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  LinearParams probe;
+  std::memset(&probe, 0, sizeof(probe));
+  probe.pdl = pdl_enabled() ? 1 : 0;
+  int clusters = 0;
+  cudaError_t e = mma ? launch_linear_mma(probe, tmpl, dtype, 0, cluster, smem, nullptr, &clusters)
+                      : launch_linear_core(probe, tmpl, dtype, 0, cluster, smem, nullptr, &clusters);
+  int ctas = (e == cudaSuccess && clusters > 0) ? clusters * cluster : 0;
+  if (e != cudaSuccess) cudaGetLastError();
+  if (ctas > num_sms) ctas = num_sms;  // one CTA per SM: shared memory allows no more
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = ctas;
+  return ctas;
 }
 
 int check_ptr16(const void *p, const char *what) {
@@ -392,26 +438,90 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream) {
     // ---- plan the two tiers
     const int tiles_h = (int)((a->host_cols + bn - 1) / bn);
     const int tiles_d = (int)((a->dev_cols + bn - 1) / bn);
+    // Resident CTAs of one wave for a cluster size (cudaOccupancyMaxActiveClusters).
+    auto capacity = [&](int cl) -> int {
+      const size_t sm = mma ? linear_mma_smem_bytes(tmpl, cl - 1) : linear_core_smem_bytes(tmpl, cl - 1);
+      if (sm == 0 || (int)sm > dev->max_smem_optin) return 0;
+      return max_resident_ctas(mma, tmpl, a->dtype, cl, sm, dev->num_sms);
+    };
     TierPlan ph, pd;
-    if (a->host_ctas > 0 || a->dev_ctas > 0) {
-      ph = user_plan(a->host_ctas, std::max(1, a->host_ksplit), tiles_h, nkb, max_ks);
-      pd = user_plan(a->dev_ctas, std::max(1, a->dev_ksplit), tiles_d, nkb, max_ks);
-      if (tiles_h > 0 && ph.ctas == 0) ph = user_plan(1, 1, tiles_h, nkb, max_ks);
-      if (tiles_d > 0 && pd.ctas == 0) pd = user_plan(1, 1, tiles_d, nkb, max_ks);
-    } else {
-      const int hb = tiles_h > 0 ? std::min(kAutoHostCtas, dev->num_sms / 2) : 0;
-      ph = auto_plan(hb, tiles_h, nkb, max_ks);
-      pd = auto_plan(dev->num_sms - ph.ctas, tiles_d, nkb, max_ks);
+    int cluster = 1;
+    // Largest split factor whose split-K receive buffer still fits with at
+    // least two pipeline stages.
+    int ks_cap = 1;
+    for (int ks = 2; ks <= max_ks; ks *= 2) {
+      const size_t sm = mma ? linear_mma_smem_bytes(tmpl, ks - 1) : linear_core_smem_bytes(tmpl, ks - 1);
+      if (sm == 0 || (int)sm > dev->max_smem_optin) break;
+      ks_cap = ks;
     }
-    int cluster = std::max(ph.ksplit, pd.ksplit);
-    if (cluster % ph.ksplit != 0 || cluster % pd.ksplit != 0) {
-      // Incompatible split factors share one launch shape: fall back to no split.
-      ph.ksplit = pd.ksplit = 1;
-      cluster = 1;
+    if (a->host_ctas > 0 || a->dev_ctas > 0) {
+      ph = user_plan(a->host_ctas, std::max(1, a->host_ksplit), tiles_h, nkb, ks_cap);
+      pd = user_plan(a->dev_ctas, std::max(1, a->dev_ksplit), tiles_d, nkb, ks_cap);
+      if (tiles_h > 0 && ph.ctas == 0) ph = user_plan(1, 1, tiles_h, nkb, ks_cap);
+      if (tiles_d > 0 && pd.ctas == 0) pd = user_plan(1, 1, tiles_d, nkb, ks_cap);
+      cluster = std::max(ph.ksplit, pd.ksplit);
+      if (cluster % ph.ksplit != 0 || cluster % pd.ksplit != 0) {
+        // Incompatible split factors share one launch shape: fall back to no split.
+        ph.ksplit = pd.ksplit = 1;
+        cluster = 1;
+      }
+    } else {
+      const int hb = tiles_h > 0 ? std::min(kAutoHostCtas, dev->num_sms / 4) : 0;
+      ph = auto_plan(hb, tiles_h, nkb, ks_cap);
+      cluster = ph.ksplit;
+      if (tiles_d > 0) {
+        // Device-tier plan, from measurements of these kernels on B200: give
+        // each group whole tiles (full-width stages stream fastest) and split
+        // K only as far as needed to bring about 1 MB of weight per CTA (at
+        // least 64 CTAs), because every split adds a DSMEM reduction per tile.
+        // With at least 3/4 of a wave of tiles, no split: tiles are spread
+        // evenly over the resident CTAs.
+        long best_cost = -1;
+        TierPlan best;
+        int best_cluster = cluster;
+        const int boxes_d = (int)((a->dev_cols + kBoxCols - 1) / kBoxCols);
+        const int bpt = bn / kBoxCols;  // boxes per full tile
+        const int tiles_full = (boxes_d + bpt - 1) / bpt;
+        const double w_bytes = 2.0 * (double)a->dev_cols * (double)a->K;
+        const int cl1 = std::max(1, ph.ksplit);
+        const int cap1 = capacity(cl1) - (ph.ctas + cl1 - 1) / cl1 * cl1;
+        if (cap1 > 0 && ph.ksplit == 1 && 4 * tiles_full >= 3 * cap1) {
+          const int per = (tiles_full + cap1 - 1) / cap1;  // tiles per group
+          best.ksplit = 1;
+          best.ctas = (tiles_full + per - 1) / per;
+          best_cluster = 1;
+          best_cost = 0;
+        } else {
+          const int target = std::max(64, (int)(w_bytes / 1.0e6));
+          for (int ks = 1; ks <= ks_cap && ks <= std::max(1, nkb); ks *= 2) {
+            const int cl = std::max(ks, ph.ksplit);
+            const int cap = capacity(cl) - (ph.ctas + cl - 1) / cl * cl;
+            const int groups = std::min(cap / ks, tiles_full);
+            if (groups <= 0) continue;
+            best.ksplit = ks;
+            best.ctas = groups * ks;
+            best_cluster = cl;
+            best_cost = 0;
+            if (best.ctas >= target || groups < tiles_full) break;
+          }
+        }
+        if (best_cost < 0) {  // no occupancy answer: one tile per CTA, no split
+          best = auto_plan(std::max(1, dev->num_sms - ph.ctas), tiles_d, nkb, 1);
+          best_cluster = ph.ksplit;
+        }
+        pd = best;
+        cluster = best_cluster;
+      }
     }
     const int span_h = (ph.ctas + cluster - 1) / cluster * cluster;
     const int span_d = (pd.ctas + cluster - 1) / cluster * cluster;
     const int grid = span_h + span_d;
+    if (trace_plans())
+      fprintf(stderr,
+              "[dak plan] %s ntok=%lld K=%lld host_cols=%lld dev_cols=%lld | host ctas=%d ks=%d | dev ctas=%d ks=%d"
+              " | cluster=%d grid=%d cap=%d\n",
+              mma ? "tcgen05" : "core", (long long)nt, (long long)a->K, (long long)a->host_cols,
+              (long long)a->dev_cols, ph.ctas, ph.ksplit, pd.ctas, pd.ksplit, cluster, grid, capacity(cluster));
 
     LinearParams p;
     std::memset(&p, 0, sizeof(p));
@@ -433,7 +543,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream) {
     }
     const void *x = static_cast<const uint16_t *>(a->x) + t0 * a->ldx;
     if (mma)
-      st = tile_map_2d(&p.xmap, x, a->dtype, nt, a->K, a->ldx, kMmaBK, tmpl, 128);
+      st = tile_map_2d(&p.xmap, x, a->dtype, nt, a->K, a->ldx, kBoxCols, tmpl, 128);  // two 64-wide boxes per stage
     else
       st = tile_map_2d(&p.xmap, x, a->dtype, nt, a->K, a->ldx, kCoreBK, tmpl, 0);
     if (st) return st;
@@ -443,6 +553,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream) {
     p.K = (int)a->K;
     p.status = dev->status;
     p.red_slots = cluster - 1;
+    p.pdl = pdl_enabled() ? 1 : 0;
 
     size_t smem;
     cudaError_t e;
@@ -454,6 +565,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream) {
                     tmpl, cluster);
       e = launch_linear_mma(p, tmpl, a->dtype, grid, cluster, smem, stream);
     } else {
+      p.stages = linear_core_stages(tmpl, cluster - 1);
       smem = linear_core_smem_bytes(tmpl, cluster - 1);
       if (smem == 0 || (int)smem > dev->max_smem_optin)
         return fail(DAK_ERR_UNSUPPORTED, "linear: shared memory plan exceeds the device limit");

@@ -10,7 +10,9 @@ def linear(x: np.ndarray, w: np.ndarray, acc=np.float64) -> np.ndarray:
     """y = x @ w.T with w [N_out, K] as nn.Linear stores it, accumulated in
     ``acc`` (the reference's check is nn.Linear, benchmark/benchmark_linear.py:121-123;
     its kernels compute C[N, M] = B[N, K] . A[K, M], include/task/gemv.cuh:267-368)."""
-    return (x.astype(acc) @ w.astype(acc).T).astype(np.float32)
+    xa = np.asarray(x, dtype=acc)
+    wa = np.asarray(w, dtype=acc)  # no copy when the weights are already stored in `acc`
+    return (xa @ wa.T).astype(np.float32, copy=False)
 
 
 def split_horizontal(m: int, ratio: float, tile_m: int = TILE_M) -> tuple[int, int]:
