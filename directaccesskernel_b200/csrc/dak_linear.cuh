@@ -17,12 +17,14 @@ constexpr int kBoxCols = 64;  // 64 x 16-bit = 128 B = one 128-byte swizzle span
 
 // ---- CUDA-core decode kernel (ntok <= 8) ---------------------------------
 // Stage shapes follow a measured rule of this part: TMA streams a [K, N]
-// weight at 6.4-6.5 TB/s with boxes of 64 x 64 (8 KB) and four adjacent boxes
-// per row (512 contiguous bytes), but at 3.5 TB/s with 64 x 32 boxes.
-constexpr int kCoreBN = 256;                      // output features per tile (4 boxes)
+// weight at 6.0-6.5 TB/s with boxes of 8-16 KB (64 x 64 or 64 x 128), but at
+// 3.5 TB/s with 4 KB boxes.  Both kernels use 128-feature x 128-row stages (two
+// 16 KB boxes), so narrow layers still have enough whole tiles to spread.
+constexpr int kCoreBN = 128;                      // output features per tile (2 boxes)
 constexpr int kCoreBoxes = kCoreBN / kBoxCols;    // TMA boxes per stage
-constexpr int kCoreBK = 64;                       // K rows per stage (8 KB boxes)
+constexpr int kCoreBK = 128;                      // K rows per stage (16 KB boxes)
 constexpr int kCoreStages = 6;                    // most weight stages (32 KB each)
+static_assert(kCoreBoxes == 2 && kCoreBK == 128, "the consumer warp map covers 2 boxes x 2 row halves of 64");
 constexpr int kCoreConsumerWarps = 8;
 constexpr int kCoreThreads = (kCoreConsumerWarps + 1) * 32;
 constexpr int kCoreMaxTok = 8;

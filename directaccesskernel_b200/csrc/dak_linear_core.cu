@@ -4,18 +4,19 @@
 // Replaces the reference's `gemv` / `gemv_horizontal` (include/task/gemv.cuh:
 // 267-452), which feed wgmma with FP16 accumulation on sm_90a.  Here:
 //   * one CTA = 1 producer warp + 8 consumer warps;
-//   * the producer streams 256-feature x 64-row weight stages (4 TMA boxes of
-//     64 x 64, 128-byte swizzle) and the matching activation slice through an
+//   * the producer streams 128-feature x 128-row weight stages (2 TMA boxes of
+//     64 x 128, 128-byte swizzle) and the matching activation slice through an
 //     mbarrier ring sized to the shared memory; the host tier's CTAs read
 //     pinned host memory over the host link, the device tier's CTAs read HBM,
 //     in the same launch;
 //   * each group of `ksplit` CTAs owns a contiguous, evenly sized range of
 //     64-feature boxes (so no group has more than one box above the average)
-//     and walks it as tiles of up to 4 boxes; the CTAs of the group split K;
-//   * consumer warp w owns 32 features of the tile; lane (q, ro) = (lane & 3,
-//     lane >> 2) reads 16 bytes of rows ro, ro+8, ... and keeps FP32 partial
-//     sums for 8 features x NTOK tokens; a 3-step xor shuffle sums the 8 row
-//     groups (the warp-shuffle reduction);
+//     and walks it as tiles of up to 2 boxes; the CTAs of the group split K;
+//   * consumer warp w = (kq, hc, b) owns 32 features (box b, 64-byte half hc)
+//     over the row half kq of every stage; lane (q, ro) reads 16 bytes of rows
+//     ro, ro+8, ... and keeps FP32 partial sums for 8 features x NTOK tokens; a
+//     3-step xor shuffle sums the 8 row groups (the warp-shuffle reduction) and
+//     the two row halves meet in shared memory;
 //   * the K-split partials of a tile are summed in the leader CTA's shared
 //     memory through DSMEM stores and remote mbarrier arrivals (no global
 //     scratch, no atomics);
@@ -32,22 +33,26 @@ namespace dak {
 namespace {
 
 constexpr uint32_t kCoreWStageBytes = kCoreBN * kCoreBK * 2;   // 32 KB
-constexpr uint32_t kCoreBoxBytes = kBoxCols * kCoreBK * 2;     // 8 KB
+constexpr uint32_t kCoreBoxBytes = kBoxCols * kCoreBK * 2;     // 16 KB
 constexpr uint32_t kCoreSmemBudget = 227 * 1024;
+constexpr int kCoreRowHalf = kCoreBK / 2;                      // rows per consumer row half
+constexpr int kCoreReduceWarps = kCoreConsumerWarps / 2;       // row-half-0 warps own the outputs
 
 template <int NTOK>
 struct CoreLayout {
   static constexpr uint32_t x_stage_bytes = NTOK * kCoreBK * 2;
   static constexpr uint32_t x_stage_stride = (x_stage_bytes + 127) & ~127u;
   static constexpr uint32_t red_slot_floats = NTOK * kCoreBN;
+  static constexpr uint32_t comb_floats = NTOK * kCoreBN;  // one row-half hand-off buffer
   int stages;
-  uint32_t w_off, x_off, bar_off, flag_off, red_off;
+  uint32_t w_off, x_off, bar_off, flag_off, comb_off, red_off;
   __host__ __device__ explicit CoreLayout(int s) : stages(s) {
     w_off = 0;
     x_off = w_off + (uint32_t)s * kCoreWStageBytes;
     bar_off = x_off + (uint32_t)s * x_stage_stride;
     flag_off = bar_off + (uint32_t)(2 * s + 2) * 8;  // full[S], empty[S], red_full, red_free
-    red_off = (flag_off + 16 + 15) & ~15u;
+    comb_off = (flag_off + 16 + 15) & ~15u;
+    red_off = comb_off + 2 * comb_floats * 4;        // double-buffered by tile parity
   }
   __host__ __device__ uint32_t bytes(int red_slots) const {
     return red_off + (uint32_t)red_slots * red_slot_floats * 4 + 1024;  // +1024: base alignment
@@ -103,8 +108,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, kCoreConsumerWarps);
     }
-    mbar_init(red_full, (uint32_t)(ks > 1 ? (ks - 1) * kCoreConsumerWarps * 32 : 1));
-    mbar_init(red_free, kCoreConsumerWarps);
+    mbar_init(red_full, (uint32_t)(ks > 1 ? (ks - 1) * kCoreReduceWarps * 32 : 1));
+    mbar_init(red_free, kCoreReduceWarps);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -169,11 +174,18 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
   } else {
     // ----------------------------------------------------------- consumers
     griddep_wait();  // y may still be read by the previous kernel of the stream
-    const int b = warp >> 1;           // TMA box (64 features) of this warp
+    const int b = warp & 1;            // TMA box (64 features) of this warp
+    const int hc = (warp >> 1) & 1;    // 64-byte half of the box's 128-byte rows
+    const int kq = warp >> 2;          // row half of every stage
     const int q = lane & 3;            // 16-byte chunk within the warp's 64 bytes
-    const int ro = lane >> 2;          // row offset 0..7 inside each 8-row group
-    const int c = (warp & 1) * 4 + q;  // logical 16-byte chunk in the 128-byte row
+    // Row offset 0..7 inside each 8-row group.  The 8 lanes of one shared-memory
+    // phase read rows ro and ro ^ 4, whose swizzled chunks fill complementary
+    // halves of the 32 banks, so the weight reads are conflict free.
+    const int ro = ((lane >> 3) & 3) | (((lane >> 2) & 1) << 2);
+    const int c = hc * 4 + q;          // logical 16-byte chunk in the 128-byte row
     const uint32_t chunk_off = (uint32_t)((c ^ ro) << 4);  // 128-byte swizzle: chunk ^ (row & 7)
+    const int row0 = kq * kCoreRowHalf;
+    float *comb = reinterpret_cast<float *>(smem + L.comb_off);
     const uint32_t my_rank = cluster_ctarank();
     int nred = 0;
     int item = 0;
@@ -195,8 +207,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
           const uint8_t *wst = smem + L.w_off + s * kCoreWStageBytes + b * kCoreBoxBytes;
           const uint16_t *xst = reinterpret_cast<const uint16_t *>(smem + L.x_off + s * L.x_stage_stride);
 #pragma unroll
-          for (int i = 0; i < kCoreBK / 8; ++i) {
-            const int row = ro + 8 * i;
+          for (int i = 0; i < kCoreRowHalf / 8; ++i) {
+            const int row = row0 + ro + 8 * i;
             const uint4 wv = *reinterpret_cast<const uint4 *>(wst + row * 128 + chunk_off);
             float wf[8];
             {
@@ -239,53 +251,70 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
           for (int jj = 0; jj < 8; ++jj) out[jj] = acc[t][jj];
 
       const int fcol = b * kBoxCols + c * 8;  // feature within the tile
-      bool write_out = true;
-      if (ks > 1) {
-        if (r > 0) {
-          // Member: push the partial into the leader's slot r-1.
-          if (nred > 0) mbar_wait<true>(red_free, (uint32_t)((nred - 1) & 1), wc);
-          const uint32_t leader = my_rank - (uint32_t)r;
-          if (ro < NTOK) {
-            const uint32_t dst = mapa_shared(
-                smem_u32(red + (size_t)(r - 1) * L.red_slot_floats + ro * kCoreBN + fcol), leader);
-            st_cluster_v4(dst, out[0], out[1], out[2], out[3]);
-            st_cluster_v4(dst + 16, out[4], out[5], out[6], out[7]);
-          }
-          mbar_arrive_remote(mapa_shared(red_full, leader));
-          write_out = false;
-        } else {
-          // Leader: add the members' partials once all of them have landed.
-          mbar_wait<true>(red_full, (uint32_t)(nred & 1), wc);
-          if (ro < NTOK) {
-            for (int m = 0; m < ks - 1; ++m) {
-              const float *src = red + (size_t)m * L.red_slot_floats + ro * kCoreBN + fcol;
-              const float4 a0 = *reinterpret_cast<const float4 *>(src);
-              const float4 a1 = *reinterpret_cast<const float4 *>(src + 4);
-              out[0] += a0.x; out[1] += a0.y; out[2] += a0.z; out[3] += a0.w;
-              out[4] += a1.x; out[5] += a1.y; out[6] += a1.z; out[7] += a1.w;
-            }
-          }
-          __syncwarp();
-          if (lane == 0)
-            for (int m = 1; m < ks; ++m) mbar_arrive_remote(mapa_shared(red_free, my_rank + m));
-        }
-        ++nred;
+      // Row half 1 hands its sums to row half 0 through a buffer chosen by tile
+      // parity; the barrier of tile j + 1 keeps tile j's buffer until it is read.
+      float *cb = comb + (size_t)(j & 1) * L.comb_floats + ro * kCoreBN + fcol;
+      if (kq == 1 && ro < NTOK) {
+        *reinterpret_cast<float4 *>(cb) = make_float4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<float4 *>(cb + 4) = make_float4(out[4], out[5], out[6], out[7]);
       }
+      named_sync(1, kCoreConsumerWarps * 32);
+      if (kq == 0) {
+        if (ro < NTOK) {
+          const float4 h0 = *reinterpret_cast<const float4 *>(cb);
+          const float4 h1 = *reinterpret_cast<const float4 *>(cb + 4);
+          out[0] += h0.x; out[1] += h0.y; out[2] += h0.z; out[3] += h0.w;
+          out[4] += h1.x; out[5] += h1.y; out[6] += h1.z; out[7] += h1.w;
+        }
 
-      if (write_out && active && ro < p.ntok) {
-        const int col = tile_box0(j) * kBoxCols + fcol;
-        if (col < tier.cols) {
-          T *yrow = reinterpret_cast<T *>(p.y) + (long long)ro * p.ldy + tier.col_offset + col;
-          if (col + 8 <= tier.cols && (reinterpret_cast<uintptr_t>(yrow) & 15u) == 0) {
-            uint4 v;
-            v.x = Elem<T>::pack2(out[0], out[1]);
-            v.y = Elem<T>::pack2(out[2], out[3]);
-            v.z = Elem<T>::pack2(out[4], out[5]);
-            v.w = Elem<T>::pack2(out[6], out[7]);
-            *reinterpret_cast<uint4 *>(yrow) = v;
+        bool write_out = true;
+        if (ks > 1) {
+          if (r > 0) {
+            // Member: push the partial into the leader's slot r-1.
+            if (nred > 0) mbar_wait<true>(red_free, (uint32_t)((nred - 1) & 1), wc);
+            const uint32_t leader = my_rank - (uint32_t)r;
+            if (ro < NTOK) {
+              const uint32_t dst = mapa_shared(
+                  smem_u32(red + (size_t)(r - 1) * L.red_slot_floats + ro * kCoreBN + fcol), leader);
+              st_cluster_v4(dst, out[0], out[1], out[2], out[3]);
+              st_cluster_v4(dst + 16, out[4], out[5], out[6], out[7]);
+            }
+            mbar_arrive_remote(mapa_shared(red_full, leader));
+            write_out = false;
           } else {
-            uint16_t *yr = reinterpret_cast<uint16_t *>(yrow);
-            for (int jj = 0; jj < 8 && col + jj < tier.cols; ++jj) yr[jj] = Elem<T>::from_float(out[jj]);
+            // Leader: add the members' partials once all of them have landed.
+            mbar_wait<true>(red_full, (uint32_t)(nred & 1), wc);
+            if (ro < NTOK) {
+              for (int m = 0; m < ks - 1; ++m) {
+                const float *src = red + (size_t)m * L.red_slot_floats + ro * kCoreBN + fcol;
+                const float4 a0 = *reinterpret_cast<const float4 *>(src);
+                const float4 a1 = *reinterpret_cast<const float4 *>(src + 4);
+                out[0] += a0.x; out[1] += a0.y; out[2] += a0.z; out[3] += a0.w;
+                out[4] += a1.x; out[5] += a1.y; out[6] += a1.z; out[7] += a1.w;
+              }
+            }
+            __syncwarp();
+            if (lane == 0)
+              for (int m = 1; m < ks; ++m) mbar_arrive_remote(mapa_shared(red_free, my_rank + m));
+          }
+          ++nred;
+        }
+
+        if (write_out && active && ro < p.ntok) {
+          const int col = tile_box0(j) * kBoxCols + fcol;
+          if (col < tier.cols) {
+            T *yrow = reinterpret_cast<T *>(p.y) + (long long)ro * p.ldy + tier.col_offset + col;
+            if (col + 8 <= tier.cols && (reinterpret_cast<uintptr_t>(yrow) & 15u) == 0) {
+              uint4 v;
+              v.x = Elem<T>::pack2(out[0], out[1]);
+              v.y = Elem<T>::pack2(out[2], out[3]);
+              v.z = Elem<T>::pack2(out[4], out[5]);
+              v.w = Elem<T>::pack2(out[6], out[7]);
+              *reinterpret_cast<uint4 *>(yrow) = v;
+            } else {
+              uint16_t *yr = reinterpret_cast<uint16_t *>(yrow);
+              for (int jj = 0; jj < 8 && col + jj < tier.cols; ++jj) yr[jj] = Elem<T>::from_float(out[jj]);
+            }
           }
         }
       }
