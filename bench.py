@@ -37,6 +37,15 @@ LLAMA8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 4096), "do
 TOKENS = (1, 4, 16, 64)
 RATIOS = (0.0, 0.25, 0.5, 0.75, 1.0)
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch divided by
+# the launch's device-tier bytes ((1 - r) W + x + y), from full-size ncu captures
+# of the Llama-3-8B layers at r = 0 and 0.5 (profiles/linear_core_llama8b_m1.md,
+# profiles/linear_mma_llama8b_m16.md): 1.000-1.004, mean 1.002.  The host tier's
+# bytes cross PCIe and never touch DRAM.
+DRAM_PER_DEVICE_BYTE = 1.002
+# Same for the attention kernel (profiles/attn_decode_config3.md): 541.6 MB of
+# DRAM traffic for 536.9 MB of device-resident K/V.
+ATTN_DRAM_PER_DEVICE_BYTE = 1.0088
 
 
 def parse_args():
@@ -326,9 +335,11 @@ def run_linear(args, torch, rank, world):
     # Roofline per launch: max((1-r) W / HBM, r W / host); x and y bytes ride with HBM.
     roof_ms = 0.0
     alg_bytes = 0
+    dram_bytes = 0.0
     per_ratio = {}
     for i, (l, m) in enumerate(calls):
         io = (m * l["k"] + m * l["n"]) * 2
+        dram_bytes += (l["w_bytes"] - l["host_bytes"] + io) * DRAM_PER_DEVICE_BYTE
         t_roof = max((l["w_bytes"] - l["host_bytes"] + io) / (hbm_gbs * 1e9),
                      l["host_bytes"] / (host_gbs * 1e9)) * 1e3
         roof_ms += t_roof * args.steps
@@ -367,7 +378,12 @@ def run_linear(args, torch, rank, world):
                              "per-launch breakdown: per-layer graphs back to back with events between",
                    "parallelism": f"replicas x{world} (weak, no collective)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": round(peak_eff, 2), "unit": "GB/s",
-                     "frac": round(achieved / peak_eff, 4), "traffic": None,
+                     "frac": round(achieved / peak_eff, 4),
+                     "traffic": round(dram_bytes / len(calls)),
+                     "traffic_basis": "DRAM bytes per launch, step average: ncu dram read+write = "
+                                      f"{DRAM_PER_DEVICE_BYTE} x device-tier bytes on full-size captures; the "
+                                      "host tier's bytes cross PCIe, so traffic < algorithmic bytes "
+                                      f"({round(alg_bytes / len(calls))} per launch)",
                      "peak_model": "combined HBM + host-link roofline, sum over layers of max((1-r)W/HBM, rW/host)",
                      "hbm_gbs": hbm_gbs, "hbm_peak_kind": peak_kind, "host_link_gbs": round(host_gbs, 2),
                      "host_link_dma_gbs": round(dma_gbs, 2), "host_link_tma_probe_gbs": round(tma_host_gbs, 2),
@@ -480,7 +496,9 @@ def run_attention(args, torch, rank, world):
                    "split_size": split, "l2": "1 GiB of KV per step exceeds L2"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2),
                      "peak": round(kv_bytes / (roof_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                     "frac": round(roof_ms * args.steps / ms, 4), "traffic": None,
+                     "frac": round(roof_ms * args.steps / ms, 4),
+                     "traffic": round((kv_bytes - host_bytes) * ATTN_DRAM_PER_DEVICE_BYTE),
+                     "traffic_basis": "ncu dram read+write of one full-size launch (profiles/attn_decode_config3.md)",
                      "peak_model": "max(device KV / HBM, host KV / host link)", "hbm_gbs": hbm_gbs,
                      "hbm_peak_kind": peak_kind, "host_link_gbs": round(host_gbs, 2)},
         "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),

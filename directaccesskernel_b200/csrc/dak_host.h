@@ -37,17 +37,19 @@ cudaError_t launch_linear_mma(const LinearParams &p, int ntok_tmpl, int dtype, i
                               int cluster, size_t smem, cudaStream_t stream,
                               int *max_clusters = nullptr);
 
+// Sets, once per kernel and device, the kernel's dynamic shared-memory limit
+// to the device's opt-in maximum and allows non-portable cluster sizes.  Every
+// launch of the kernel, of any size, then fits the function's attributes, also
+// when a captured graph node is launched again on its own.
+cudaError_t prepare_kernel_attributes(const void *kern);
+
 // Launch (or, with grid == 0, occupancy query) of a linear kernel: 1-D grid,
 // 1-D clusters, programmatic stream serialization when p.pdl is set.
 template <typename Kern>
 cudaError_t launch_linear_kernel(Kern kern, const LinearParams &p, int grid, int threads, int cluster,
                                  size_t smem, cudaStream_t stream, int *max_clusters) {
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = prepare_kernel_attributes(reinterpret_cast<const void *>(kern));
   if (e != cudaSuccess) return e;
-  if (cluster > 8) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid > 0 ? grid : cluster);
   cfg.blockDim = dim3(threads);

@@ -12,8 +12,10 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
 #include <string>
 #include <unordered_map>
+#include <utility>
 
 #include "dak_common.cuh"
 #include "dak_host.h"
@@ -84,6 +86,22 @@ int device_info(DeviceInfo **out) {
 int *device_status_word() {
   DeviceInfo *d = nullptr;
   return device_info(&d) == DAK_OK ? d->status : nullptr;
+}
+
+cudaError_t prepare_kernel_attributes(const void *kern) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void *>> done;
+  DeviceInfo *d = nullptr;
+  if (device_info(&d) != DAK_OK) return cudaErrorInvalidDevice;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({dev, kern})) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->max_smem_optin);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) done.insert({dev, kern});
+  return e;
 }
 
 // A kernel may only be pointed at memory of the current device or at pinned
