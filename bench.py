@@ -54,7 +54,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["linear", "attention"], default="linear")
+    ap.add_argument("--workload", choices=["linear", "attention", "opt66b"], default="linear")
+    ap.add_argument("--hbm-budget-gb", type=float, default=96.0, help="opt66b: HBM weight budget (GB)")
+    ap.add_argument("--prompt-len", type=int, default=512, help="opt66b: prompt tokens")
     ap.add_argument("--tokens", type=str, default=None, help="comma list overriding the M sweep")
     ap.add_argument("--ratios", type=str, default=None, help="comma list overriding the ratio sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -485,6 +487,29 @@ def run_attention(args, torch, rank, world):
     ms = e0.elapsed_time(e1)
     kv_bytes = 2 * B * Hkv * S * 128 * 2
     host_bytes = kv_bytes // 2
+
+    # End to end: the query comes from pinned host memory and the output goes back
+    # to it every step.
+    q_host = q.cpu().pin_memory()
+    o_host = torch.empty_like(out, device="cpu").pin_memory()
+
+    def step_e2e():
+        q.copy_(q_host, non_blocking=True)
+        step()
+        o_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step_e2e()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        step_e2e()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_attention()
     roof_ms = max((kv_bytes - host_bytes) / (hbm_gbs * 1e9), host_bytes / (host_gbs * 1e9)) * 1e3
     achieved = kv_bytes * args.steps / (ms * 1e-3) / 1e9
     return {
@@ -501,8 +526,148 @@ def run_attention(args, torch, rank, world):
                      "traffic_basis": "ncu dram read+write of one full-size launch (profiles/attn_decode_config3.md)",
                      "peak_model": "max(device KV / HBM, host KV / host link)", "hbm_gbs": hbm_gbs,
                      "hbm_peak_kind": peak_kind, "host_link_gbs": round(host_gbs, 2)},
+        "e2e": {"value": round(world * kv_bytes * args.steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": q_host.numel() * 2, "d2h_bytes_per_step": o_host.numel() * 2},
         "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+        **({"cpu_baseline": cpu} if cpu is not None else {}),
     }
+
+
+def cpu_baseline_attention(budget_s: float = 15.0):
+    """The oracle port of the attention (numpy FP32 softmax attention per GQA
+    group, BLAS matrix products on all host threads) on a bounded sample of
+    config 3: whole sequences of 32768 tokens, all 8 KV heads, one at a time."""
+    import numpy as np
+
+    import oracle.attention as oatt
+
+    rng = np.random.default_rng(0)
+    Hq, Hkv, S, D = 32, 8, 32768, 128
+    k = rng.standard_normal((1, Hkv, S, D), dtype=np.float32)
+    v = rng.standard_normal((1, Hkv, S, D), dtype=np.float32)
+    t_total, seqs = 0.0, 0
+    while t_total < budget_s and seqs < 64:
+        q = rng.standard_normal((1, Hq, 1, D), dtype=np.float32)
+        t = time.perf_counter()
+        oatt.decode_attention_grouped(q, k, v, 1.0 / math.sqrt(D))
+        t_total += time.perf_counter() - t
+        seqs += 1
+    kv_fp16 = 2 * Hkv * S * D * 2 * seqs
+    return {"value": round(kv_fp16 / t_total / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{seqs} whole sequences (ctx {S}, Hq {Hq} / Hkv {Hkv}, D {D}) of config 3; "
+                      "fp16 KV bytes / numpy FP32 time"}
+
+
+# ------------------------------------------------------------ opt66b decode
+OPT66B_LINEARS_PER_LAYER = 6  # q, k, v, out_proj, fc1, fc2
+
+
+def run_opt66b(args, torch, rank, world):
+    """OPT-66B architecture (random N(0, 0.02) fp16 weights, 131.4 GB)
+    under an HBM weight budget; the placement puts the rest of the decoder linears in
+    pinned host memory.  Batch 1, a random 512-token prompt, greedy decode with one
+    CUDA graph per step (benchmark_opt.py:137-460).  Metric: decode tokens/s."""
+    if world > 1:
+        raise SystemExit("the opt66b workload runs on one GPU (BASELINE config 4); it pins ~35 GB of host "
+                         "memory per process")
+    from directaccesskernel_b200 import decode, runtime
+
+    hbm_gbs, peak_kind = measured_peaks()
+    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime)
+    host_gbs = max(dma_gbs, tma_host_gbs)
+    cfg = decode.opt_config("opt-66b")
+    budget = int(args.hbm_budget_gb * 1e9)
+    t0 = time.perf_counter()
+    model, stats = decode.build_offloaded_model(cfg, linear_type="horizontal", hbm_budget_bytes=budget, seed=rank)
+    build_s = time.perf_counter() - t0
+    B, L = 1, args.prompt_len
+    W, K = max(3, args.warmup), args.steps
+    prompt = decode.random_prompt(B, L, cfg.vocab_size, seed=0)
+    dec = decode.GreedyDecoder(model, B, L + W + 2 * K + 8, graph=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        res = dec.generate(prompt, W + K, warmup_steps=W)
+    tbt = res.tbt_ms
+    model_bytes = stats.host_bytes + stats.device_bytes
+    roof_ms = decode.decode_roofline_ms(stats, hbm_gbs, host_gbs)
+    status = runtime.device_status()
+    if status != 0:
+        raise RuntimeError(f"device error word {status} after the timed region")
+
+    # End to end: every step the token goes to pinned host memory and comes back as
+    # the next step's input, as a serving loop that streams tokens out does.
+    tok_host = torch.empty(B, 1, dtype=torch.long).pin_memory()
+    tok_host.copy_(res.tokens[:, -1:])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.inference_mode():
+        e0.record()
+        for _ in range(K):
+            dec.ids.copy_(tok_host, non_blocking=True)
+            logits = dec.step()
+            nxt = torch.argmax(logits, dim=-1)
+            tok_host.copy_(nxt[:, None], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            dec.advance(logits, forced=nxt)
+        e1.record()
+        torch.cuda.synchronize()
+    e2e_tbt = e0.elapsed_time(e1) / K
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_opt66b()
+    n_layers = cfg.num_hidden_layers
+    return {
+        "metric": "decode tokens/s (OPT-66B arch, HBM weight budget)", "value": round(B * 1e3 / tbt, 4),
+        "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(tbt, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+        "data": "synthetic: random N(0,0.02) weights, random prompt ids",
+        "config": {"workload": f"BASELINE config 4: OPT-66B arch, HBM budget {args.hbm_budget_gb:g} GB, batch {B}, "
+                               f"prompt {L}, greedy decode", "model_bytes": model_bytes,
+                   "host_bytes": stats.host_bytes, "device_bytes": stats.device_bytes,
+                   "weight_offload_ratio": round(stats.actual_offload_ratio, 4), "build_s": round(build_s, 1),
+                   "prefill_ms": round(res.prefill_ms, 1), "l2": "131 GB of weights per step exceed L2",
+                   "timing": "CUDA events around each graph replay of one decode step"},
+        "roofline": {"bound": "hbm", "achieved": round(model_bytes / (tbt * 1e-3) / 1e9, 2),
+                     "peak": round(model_bytes / (roof_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                     "frac": round(roof_ms / tbt, 4),
+                     "traffic": round(stats.device_bytes * DRAM_PER_DEVICE_BYTE),
+                     "traffic_basis": "per decode step: device-resident weight bytes x the DRAM/device-byte ratio "
+                                      "of the linear captures",
+                     "peak_model": "max(device weight bytes / HBM, host weight bytes / host link) per step",
+                     "hbm_gbs": hbm_gbs, "hbm_peak_kind": peak_kind, "host_link_gbs": round(host_gbs, 2),
+                     "host_link_dma_gbs": round(dma_gbs, 2), "host_link_tma_probe_gbs": round(tma_host_gbs, 2)},
+        "e2e": {"value": round(B * 1e3 / e2e_tbt, 4), "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,
+                "d2h_bytes_per_step": 8 * B},
+        "gpu_launches": OPT66B_LINEARS_PER_LAYER * n_layers * K, "clocks": clocks.summary(),
+        **({"cpu_baseline": cpu} if cpu is not None else {}),
+    }
+
+
+def cpu_baseline_opt66b(reps: int = 2):
+    """The oracle port on the host cores: numpy FP32 x @ W^T of one OPT-66B decoder
+    layer's six linears at batch 1, extrapolated to the whole model by parameter
+    count (the CPU cannot hold the 263 GB FP32 model)."""
+    import numpy as np
+
+    import oracle
+
+    h, f = 9216, 36864
+    rng = np.random.default_rng(0)
+    shapes = [(h, h)] * 4 + [(f, h), (h, f)]
+    ws = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.02) for s in shapes]
+    layer_params = sum(a * b for a, b in shapes)
+    best = float("inf")
+    for _ in range(reps):
+        x = rng.standard_normal((1, h), dtype=np.float32)
+        t = time.perf_counter()
+        for w in ws:
+            y = oracle.linear(x if w.shape[1] == h else np.zeros((1, f), np.float32), w, acc=np.float32)
+        best = min(best, time.perf_counter() - t)
+        del y
+    total_params = 65_719_701_504
+    t_token = best * total_params / layer_params
+    return {"value": round(1.0 / t_token, 5), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": "one OPT-66B decoder layer (6 linears, 1.02 B params, numpy FP32, batch 1), best of "
+                      f"{reps}, extrapolated to 65.7 B params (extrapolated)"}
 
 
 def run_reference(args):
@@ -511,6 +676,26 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
+    if args.workload in ("attention", "opt66b"):
+        fn = cpu_baseline_attention if args.workload == "attention" else cpu_baseline_opt66b
+        metric, unit = (("split-KV decode attention KV GB/s", "GB/s") if args.workload == "attention" else
+                        ("decode tokens/s (OPT-66B arch, HBM weight budget)", "tokens/s"))
+        for _ in range(max(0, min(args.warmup, 1))):
+            fn() if args.workload == "opt66b" else fn(budget_s=2.0)
+        t0 = time.perf_counter()
+        runs = [fn() for _ in range(args.steps)]
+        elapsed = time.perf_counter() - t0
+        v = statistics.median(r["value"] for r in runs)
+        cpu = dict(runs[0], value=v)
+        return {
+            "metric": metric, "impl": "reference", "value": v, "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed / max(1, args.steps) * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"BASELINE {'config 3' if args.workload == 'attention' else 'config 4'} "
+                                   "sample on host cores"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
     tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else list(TOKENS)
     for _ in range(max(0, min(args.warmup, 1))):
         cpu_baseline_linear(tokens[:1], budget_s=5.0)
@@ -551,7 +736,7 @@ def main():
 
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     try:
-        fn = run_attention if args.workload == "attention" else run_linear
+        fn = {"attention": run_attention, "opt66b": run_opt66b}.get(args.workload, run_linear)
         line = fn(args, torch, rank, world)
         if rank == 0:
             print(json.dumps(line), flush=True)

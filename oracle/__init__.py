@@ -7,6 +7,6 @@ CPU path.  Each function cites the reference file:line it restates.  The oracle
 is pinned against golden vectors that tests/golden/make_golden.py produced by
 running the reference's own Python code (tests/test_oracle_golden.py).
 """
-from .attention import (batch_split_decode, decode_attention, lse_merge, paged_decode, paged_gather,  # noqa: F401
-                        split_partials)
+from .attention import (batch_split_decode, decode_attention, decode_attention_grouped, lse_merge,  # noqa: F401
+                        paged_decode, paged_gather, split_partials)
 from .linear import gemv_horizontal, horizontal_split, linear, split_horizontal  # noqa: F401

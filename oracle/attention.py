@@ -31,6 +31,25 @@ def decode_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarr
     return np.transpose(o, (0, 2, 1, 3)).astype(np.float32)
 
 
+def decode_attention_grouped(q: np.ndarray, k: np.ndarray, v: np.ndarray, scaling: float = 1.0,
+                             acc=np.float32) -> np.ndarray:
+    """``decode_attention`` without a mask, computed per GQA group with matrix
+    products instead of materialising repeat_kv: query heads j*n_rep ..
+    j*n_rep + n_rep - 1 attend to kv head j (vanila_llama.py:212-246).  Same
+    result; this is the form the host-core baseline times.
+    q [B, Hq, 1, D], k/v [B, Hkv, S, D]; returns [B, 1, Hq, D]."""
+    B, Hq, _, D = q.shape
+    Hkv = k.shape[1]
+    qg = q.astype(acc, copy=False).reshape(B, Hkv, Hq // Hkv, D)
+    kk = k.astype(acc, copy=False)
+    s = np.matmul(qg, kk.transpose(0, 1, 3, 2)) * acc(scaling)
+    s -= s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    o = np.matmul(p, v.astype(acc, copy=False))
+    return o.reshape(B, 1, Hq, D).astype(np.float32)
+
+
 def batch_split_decode(q, k_dev, v_dev, k_host, v_host, host_size: int, mask=None, scaling: float = 1.0):
     """`_C.decode` semantics (opt_attention_ext.cpp:164-319; kernel.cuh:331-348):
     rows b < host_size read the host KV, the rest the device KV (row b - host_size)."""

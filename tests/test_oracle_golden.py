@@ -71,6 +71,9 @@ def test_attention_oracle_gqa_matches_reference_llama_eager():
     assert checksum(np.concatenate([q.ravel(), k.ravel(), v.ravel()])) == str(d["gqa_sha"])
     got = oracle.decode_attention(q, k, v, None, 1.0 / math.sqrt(128))
     assert rel_err(got, d["gqa_out"]) < 1e-5
+    # The grouped-matmul form the host-core baseline times gives the same result.
+    grouped = oracle.decode_attention_grouped(q, k, v, 1.0 / math.sqrt(128))
+    assert rel_err(grouped, d["gqa_out"]) < 1e-5
 
 
 @pytest.mark.parametrize("split", [64, 100, 256, 4096])
