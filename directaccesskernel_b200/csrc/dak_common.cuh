@@ -38,6 +38,14 @@ template <> struct Elem<__half> {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&h);
   }
+  // lo += w.lo * x, hi += w.hi * x with 16-bit inputs and FP32 accumulation:
+  // the mixed-precision FMA converts its 16-bit operands exactly and rounds
+  // once, the same result as fmaf(float(w), float(x), acc).
+  static __device__ __forceinline__ void fma_pair(float &lo, float &hi, uint32_t w2, uint16_t x) {
+    asm("{\n\t.reg .b16 wl, wh;\n\tmov.b32 {wl, wh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, wl, %3, %0;\n\tfma.rn.f32.f16 %1, wh, %3, %1;\n\t}"
+        : "+f"(lo), "+f"(hi) : "r"(w2), "h"(x));
+  }
 };
 template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ float2 to_float2(uint32_t v) {
@@ -53,6 +61,11 @@ template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ uint32_t pack2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&h);
+  }
+  static __device__ __forceinline__ void fma_pair(float &lo, float &hi, uint32_t w2, uint16_t x) {
+    asm("{\n\t.reg .b16 wl, wh;\n\tmov.b32 {wl, wh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, wl, %3, %0;\n\tfma.rn.f32.bf16 %1, wh, %3, %1;\n\t}"
+        : "+f"(lo), "+f"(hi) : "r"(w2), "h"(x));
   }
 };
 

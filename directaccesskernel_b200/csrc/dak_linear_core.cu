@@ -193,6 +193,9 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
     for (int j = 0; j < ntiles && kb1 > kb0; ++j) {
       const int nbox = tile_nbox(j);
       const bool active = b < nbox;
+      // FP32 partial sums for 8 features x NTOK tokens.  Each multiply-add is one
+      // mixed-precision FMA on the 16-bit weight and activation (no conversion
+      // instructions; same rounding as fmaf on the converted values).
       float acc[NTOK][8];
 #pragma unroll
       for (int t = 0; t < NTOK; ++t)
@@ -210,18 +213,12 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
           for (int i = 0; i < kCoreRowHalf / 8; ++i) {
             const int row = row0 + ro + 8 * i;
             const uint4 wv = *reinterpret_cast<const uint4 *>(wst + row * 128 + chunk_off);
-            float wf[8];
-            {
-              const float2 f0 = Elem<T>::to_float2(wv.x), f1 = Elem<T>::to_float2(wv.y);
-              const float2 f2 = Elem<T>::to_float2(wv.z), f3 = Elem<T>::to_float2(wv.w);
-              wf[0] = f0.x; wf[1] = f0.y; wf[2] = f1.x; wf[3] = f1.y;
-              wf[4] = f2.x; wf[5] = f2.y; wf[6] = f3.x; wf[7] = f3.y;
-            }
+            const uint32_t w2[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
             for (int t = 0; t < NTOK; ++t) {
-              const float xv = Elem<T>::to_float(xst[t * kCoreBK + row]);
+              const uint16_t xh = xst[t * kCoreBK + row];
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj) acc[t][jj] = fmaf(wf[jj], xv, acc[t][jj]);
+              for (int jj = 0; jj < 4; ++jj) Elem<T>::fma_pair(acc[t][2 * jj], acc[t][2 * jj + 1], w2[jj], xh);
             }
           }
         }
