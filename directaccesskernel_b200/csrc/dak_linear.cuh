@@ -28,6 +28,12 @@ static_assert(kCoreBoxes == 2 && kCoreBK == 128, "the consumer warp map covers 2
 constexpr int kCoreConsumerWarps = 8;
 constexpr int kCoreThreads = (kCoreConsumerWarps + 1) * 32;
 constexpr int kCoreMaxTok = 8;
+// Automatic path choice: the CUDA-core kernel up to this many tokens, tcgen05
+// above.  Measured on B200 over the Llama-3-8B shapes (back-to-back launches,
+// HBM only): CUDA core 78.9 / 84.8 / 105.7 / 146.2 us at 1 / 2 / 4 / 8 tokens,
+// tcgen05 86.9 us at 16 tokens.  From 3 tokens up, the FP32 FMA work of
+// the CUDA-core kernel, not the weight stream, sets its time.
+constexpr int kCoreAutoMaxTok = 2;
 
 // ---- tcgen05 kernel (ntok up to 256) --------------------------------------
 constexpr int kMmaBM = 128;                       // UMMA M: output features per tile (2 boxes)

@@ -432,7 +432,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream) {
   if ((st = device_info(&dev))) return st;
 
   int path = a->path;
-  if (path == DAK_PATH_AUTO) path = a->ntok <= kCoreMaxTok ? DAK_PATH_CUDA_CORE : DAK_PATH_TCGEN05;
+  if (path == DAK_PATH_AUTO) path = a->ntok <= kCoreAutoMaxTok ? DAK_PATH_CUDA_CORE : DAK_PATH_TCGEN05;
   if (path == DAK_PATH_CUDA_CORE && a->ntok > kCoreMaxTok)
     return fail(DAK_ERR_INVALID_ARG, "CUDA-core path serves at most %d tokens", kCoreMaxTok);
   const bool mma = path == DAK_PATH_TCGEN05;

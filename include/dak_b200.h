@@ -166,7 +166,7 @@ DAK_API int dak_gemv_horizontal_multicast_prefill(
  * [K, dev_cols]; x is [ntok, K]; y is [ntok, *] and receives the host columns
  * at y[:, host_col_offset:...] and the device columns at y[:, dev_col_offset:...]. */
 enum dak_linear_path {
-  DAK_PATH_AUTO = 0,      /* CUDA-core for few tokens, tensor cores above    */
+  DAK_PATH_AUTO = 0,      /* CUDA-core for 1-2 tokens, tensor cores from 3    */
   DAK_PATH_CUDA_CORE = 1, /* FP32 FMA + warp-shuffle reduction, ntok <= 8     */
   DAK_PATH_TCGEN05 = 2    /* tcgen05.mma kind::f16, FP32 accumulators in TMEM */
 };
