@@ -88,6 +88,16 @@ class AttnPagedArgs(ctypes.Structure):
     ]
 
 
+class KvAppendArgs(ctypes.Structure):
+    _fields_ = [
+        ("k_new", c_vp), ("v_new", c_vp), ("new_batch_stride", c_i64), ("new_head_stride", c_i64),
+        ("k_pool_dev", c_vp), ("v_pool_dev", c_vp), ("dev_pages", c_i64),
+        ("k_pool_host", c_vp), ("v_pool_host", c_vp), ("host_pages", c_i64),
+        ("block_table", c_vp), ("table_stride", c_i64), ("max_pages", c_int), ("positions", c_vp),
+        ("batch", c_int), ("kv_heads", c_int), ("head_dim", c_int), ("page_size", c_int), ("dtype", c_int),
+    ]
+
+
 # name -> (restype, argtypes); the full list of entry points of include/dak_b200.h.
 _I64P = ctypes.POINTER(c_i64)
 SIGNATURES = {
@@ -108,6 +118,7 @@ SIGNATURES = {
     "dak_flush_l2_cache": (c_int, [c_vp, ctypes.c_size_t, c_vp, c_vp]),
     "dak_attn_decode": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_attn_decode_paged": (c_int, [ctypes.POINTER(AttnPagedArgs), c_vp]),
+    "dak_kv_append_paged": (c_int, [ctypes.POINTER(KvAppendArgs), c_vp]),
     "dak_attn_decode_noalloc": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_device_status": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "dak_selftest_wait_timeout": (c_int, [ctypes.c_uint, c_vp]),

@@ -264,6 +264,52 @@ def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_de
     return out
 
 
+def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.Tensor | None,
+                    v_pool_dev: torch.Tensor | None, k_pool_host: torch.Tensor | None,
+                    v_pool_host: torch.Tensor | None, block_table: torch.Tensor, positions: torch.Tensor) -> None:
+    """Writes k_new/v_new [B, Hkv, D] of one new token per sequence into the paged
+    pools (the layout of ``decode_paged``) at ``positions`` [B] (int32, CUDA): device
+    pages in HBM, host pages straight into pinned host memory from the GPU.
+    Replaces the reference's per-step host-cache update
+    (app/python/pinned_static_cache.py:47-107)."""
+    if k_new.shape != v_new.shape or k_new.dim() != 3 or k_new.stride(2) != 1 or v_new.stride() != k_new.stride():
+        raise RuntimeError("k_new and v_new must be [B, Hkv, D] with equal strides and a contiguous last dimension")
+    if k_new.dtype not in (torch.float16, torch.bfloat16) or v_new.dtype != k_new.dtype:
+        raise RuntimeError("k_new and v_new must be float16 or bfloat16")
+    pool = k_pool_dev if k_pool_dev is not None else k_pool_host
+    if pool is None:
+        raise RuntimeError("no KV pool given")
+    B, Hkv, D = k_new.shape
+    for t, nm, on_dev in ((k_pool_dev, "k_pool_dev", True), (v_pool_dev, "v_pool_dev", True),
+                          (k_pool_host, "k_pool_host", False), (v_pool_host, "v_pool_host", False)):
+        if t is None:
+            continue
+        if t.dim() != 4 or t.size(1) != Hkv or t.size(3) != D or not t.is_contiguous() or t.dtype != k_new.dtype:
+            raise RuntimeError(f"{nm} must be a contiguous [pages, {Hkv}, page_size, {D}] tensor of the KV dtype")
+        if t.size(2) != pool.size(2):
+            raise RuntimeError("all pools must share page_size")
+        if t.is_cuda != on_dev or (not on_dev and not t.is_pinned()):
+            raise RuntimeError(f"{nm} must be {'CUDA' if on_dev else 'pinned host'} memory")
+    if (k_pool_dev is None) != (v_pool_dev is None) or (k_pool_host is None) != (v_pool_host is None):
+        raise RuntimeError("K and V pools come in pairs")
+    if block_table.dtype != torch.int32 or not block_table.is_cuda or block_table.dim() != 2 or block_table.stride(1) != 1:
+        raise RuntimeError("block_table must be an int32 CUDA tensor [B, max_pages]")
+    if positions.dtype != torch.int32 or not positions.is_cuda or positions.numel() != B or not positions.is_contiguous():
+        raise RuntimeError("positions must be a contiguous int32 CUDA tensor [B]")
+    a = _lib.KvAppendArgs()
+    a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
+    a.new_batch_stride, a.new_head_stride = k_new.stride(0), k_new.stride(1)
+    if k_pool_dev is not None:
+        a.k_pool_dev, a.v_pool_dev, a.dev_pages = k_pool_dev.data_ptr(), v_pool_dev.data_ptr(), k_pool_dev.size(0)
+    if k_pool_host is not None:
+        a.k_pool_host, a.v_pool_host, a.host_pages = k_pool_host.data_ptr(), v_pool_host.data_ptr(), k_pool_host.size(0)
+    a.block_table, a.table_stride, a.max_pages = block_table.data_ptr(), block_table.stride(0), block_table.size(1)
+    a.positions = positions.data_ptr()
+    a.batch, a.kv_heads, a.head_dim, a.page_size = B, Hkv, D, pool.size(2)
+    a.dtype = dak_dtype(k_new.dtype)
+    check(LIB.dak_kv_append_paged(ctypes.byref(a), _stream_ptr()), "kv_append_paged")
+
+
 # ------------------------------------------------------------ Hugging Face hook
 def _pop_host_kv_kwargs(kwargs: dict):
     """interface.py:22-26."""

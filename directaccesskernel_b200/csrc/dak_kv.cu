@@ -1,0 +1,121 @@
+// dak_kv.cu - the writer side of the tiered, paged KV cache.
+//
+// Each decode step appends one token's K and V per (sequence, KV head) to the
+// page the block table names for that token: a device page in HBM or a host
+// page in pinned, mapped host memory.  The GPU writes host pages directly over
+// the host link; nothing is staged and nothing waits on the CPU.
+//
+// Replaces the reference's host-cache update (app/python/pinned_static_cache.py:
+// 47-107, fed by `.to("cpu").pin_memory()` in app/python/llama/vanila_llama.py:
+// 321-345), which copies the new K/V to the host synchronously and scatters them
+// with the CPU every step.
+#include <cstring>
+
+#include "dak_common.cuh"
+#include "dak_host.h"
+
+namespace dak {
+namespace {
+
+struct KvAppendParams {
+  const uint8_t *k_new, *v_new;
+  long long new_bs, new_hs;            // bytes
+  uint8_t *pool[2][2];                 // [k/v][device/host]
+  long long pages[2];                  // device, host
+  long long page_bytes, head_bytes;    // bytes of one page / one head's slab in a page
+  const int32_t *table;
+  long long table_stride;              // entries
+  const int32_t *positions;
+  int max_pages;                       // table entries per sequence
+  int kv_heads, row_bytes, page_size;
+  int *status;
+};
+
+// One warp per (sequence, KV head): lanes split the K row and the V row into
+// 16-byte pieces.  Out-of-range table entries or positions are recorded in the
+// status word and skipped, never written.
+__global__ void __launch_bounds__(32) kv_append_kernel(const __grid_constant__ KvAppendParams p) {
+  const int b = blockIdx.x / p.kv_heads;
+  const int h = blockIdx.x - b * p.kv_heads;
+  const int pos = p.positions[b];
+  const int page = pos / p.page_size;
+  if (pos < 0 || page >= p.max_pages) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, DAK_ERR_INVALID_ARG);
+    return;
+  }
+  const int entry = p.table[(long long)b * p.table_stride + page];
+  const int tier = entry < 0 ? 1 : 0;
+  const long long idx = entry < 0 ? -1ll - entry : entry;
+  if (idx >= p.pages[tier] || p.pool[0][tier] == nullptr) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, DAK_ERR_INVALID_ARG);
+    return;
+  }
+  const long long dst_off = idx * p.page_bytes + h * p.head_bytes + (long long)(pos - page * p.page_size) * p.row_bytes;
+  const long long src_off = b * p.new_bs + h * p.new_hs;
+  const int pieces = p.row_bytes / 16;
+  for (int i = threadIdx.x; i < 2 * pieces; i += 32) {
+    const int kv = i >= pieces ? 1 : 0;
+    const int piece = i - kv * pieces;
+    const uint8_t *src = (kv ? p.v_new : p.k_new) + src_off + piece * 16;
+    uint8_t *dst = p.pool[kv][tier] + dst_off + piece * 16;
+    *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+  }
+  // Host pages are read back over the host link by the next kernels of the
+  // stream; make the writes visible system-wide before this grid completes.
+  if (tier == 1) __threadfence_system();
+}
+
+}  // namespace
+}  // namespace dak
+
+extern "C" int dak_kv_append_paged(const dak_kv_append_args *a, void *stream) {
+  using namespace dak;
+  if (!a) return fail(DAK_ERR_INVALID_ARG, "args is null");
+  if (a->dtype != DAK_DTYPE_F16 && a->dtype != DAK_DTYPE_BF16)
+    return fail(DAK_ERR_UNSUPPORTED, "KV append supports float16 and bfloat16");
+  if (a->batch <= 0 || a->kv_heads <= 0 || a->head_dim <= 0 || a->page_size <= 0 || a->max_pages <= 0)
+    return fail(DAK_ERR_INVALID_ARG, "batch, kv_heads, head_dim, page_size and max_pages must be positive");
+  if ((a->head_dim * 2) % 16 != 0) return fail(DAK_ERR_ALIGNMENT, "head_dim must be a multiple of 8");
+  if (!a->k_new || !a->v_new || !a->block_table || !a->positions)
+    return fail(DAK_ERR_INVALID_ARG, "k_new, v_new, block_table and positions are required");
+  if (a->table_stride < a->max_pages) return fail(DAK_ERR_INVALID_ARG, "table_stride below max_pages");
+  if ((a->dev_pages > 0) != (a->k_pool_dev != nullptr && a->v_pool_dev != nullptr) ||
+      (a->host_pages > 0) != (a->k_pool_host != nullptr && a->v_pool_host != nullptr))
+    return fail(DAK_ERR_INVALID_ARG, "each tier needs both pools and a positive page count, or neither");
+  if (a->dev_pages <= 0 && a->host_pages <= 0) return fail(DAK_ERR_INVALID_ARG, "no KV pool given");
+  if ((a->new_batch_stride % 8) || (a->new_head_stride % 8))
+    return fail(DAK_ERR_ALIGNMENT, "k_new/v_new strides must be multiples of 8 elements");
+  const void *ptrs[6] = {a->k_new, a->v_new, a->k_pool_dev, a->v_pool_dev, a->k_pool_host, a->v_pool_host};
+  for (const void *q : ptrs) {
+    if (q && (reinterpret_cast<uintptr_t>(q) & 15u)) return fail(DAK_ERR_ALIGNMENT, "all buffers must be 16-byte aligned");
+    if (q) {
+      int st = check_gpu_accessible(q, "KV buffer");
+      if (st) return st;
+    }
+  }
+  KvAppendParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.k_new = static_cast<const uint8_t *>(a->k_new);
+  p.v_new = static_cast<const uint8_t *>(a->v_new);
+  p.new_bs = a->new_batch_stride * 2;
+  p.new_hs = a->new_head_stride * 2;
+  p.pool[0][0] = static_cast<uint8_t *>(a->k_pool_dev);
+  p.pool[1][0] = static_cast<uint8_t *>(a->v_pool_dev);
+  p.pool[0][1] = static_cast<uint8_t *>(a->k_pool_host);
+  p.pool[1][1] = static_cast<uint8_t *>(a->v_pool_host);
+  p.pages[0] = a->dev_pages > 0 ? a->dev_pages : 0;
+  p.pages[1] = a->host_pages > 0 ? a->host_pages : 0;
+  p.row_bytes = a->head_dim * 2;
+  p.head_bytes = (long long)a->page_size * p.row_bytes;
+  p.page_bytes = p.head_bytes * a->kv_heads;
+  p.table = a->block_table;
+  p.table_stride = a->table_stride;
+  p.positions = a->positions;
+  p.max_pages = a->max_pages;
+  p.kv_heads = a->kv_heads;
+  p.page_size = a->page_size;
+  p.status = device_status_word();
+  if (!p.status) return fail(DAK_ERR_CUDA, "no device status word");
+  kv_append_kernel<<<a->batch * a->kv_heads, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_status(cudaGetLastError(), "KV append launch");
+}

@@ -261,6 +261,32 @@ typedef struct dak_attn_paged_args {
 } dak_attn_paged_args;
 DAK_API int dak_attn_decode_paged(const dak_attn_paged_args *args, void *stream);
 
+/* Appends one token per sequence to a tiered, paged KV cache: for sequence b
+ * and KV head h, k_new[b, h, :] and v_new[b, h, :] go to slot
+ * positions[b] % page_size of page block_table[b, positions[b] / page_size],
+ * which is device page v (v >= 0) or host page -1 - v (v < 0), in the pool
+ * layout of dak_attn_decode_paged ([pages, kv_heads, page_size, head_dim]).
+ * Host pages are written by the GPU straight into pinned, mapped memory.
+ * Replaces the reference's host-cache update (app/python/pinned_static_cache.py:
+ * 47-107 with the synchronous copy at app/python/llama/vanila_llama.py:321-345).
+ * Out-of-range entries are recorded in the device error word
+ * (DAK_ERR_INVALID_ARG) and skipped.  No allocation; stream-ordered. */
+typedef struct dak_kv_append_args {
+  const void *k_new, *v_new;          /* [batch, kv_heads, head_dim]            */
+  int64_t new_batch_stride, new_head_stride;  /* elements, multiples of 8        */
+  void *k_pool_dev, *v_pool_dev;      /* device pools (or NULL)                 */
+  int64_t dev_pages;
+  void *k_pool_host, *v_pool_host;    /* pinned host pools (or NULL)            */
+  int64_t host_pages;
+  const int32_t *block_table;         /* [batch, table_stride]                  */
+  int64_t table_stride;
+  int max_pages;                      /* valid entries per table row            */
+  const int32_t *positions;           /* [batch] token index to write           */
+  int batch, kv_heads, head_dim, page_size;
+  int dtype;
+} dak_kv_append_args;
+DAK_API int dak_kv_append_paged(const dak_kv_append_args *args, void *stream);
+
 /* ------------------------------------------------------------ diagnostics */
 /* Reads (and with clear != 0 resets) the device-side error word that kernels
  * set when a bounded wait times out.  Synchronizes the current device. */

@@ -1,0 +1,114 @@
+"""The writer side of the tiered paged KV cache (dak_kv_append_paged) on the GPU:
+appends land in the right device or pinned host page, a cache built token by
+token decodes like the dense oracle, and bad table entries are recorded in the
+device error word instead of being written."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _pools(pages_dev, pages_host, hkv, P, D=128, dtype=torch.float16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    kd = torch.randn(pages_dev, hkv, P, D, generator=g).to(dtype).cuda()
+    vd = torch.randn(pages_dev, hkv, P, D, generator=g).to(dtype).cuda()
+    kh = torch.randn(pages_host, hkv, P, D, generator=g).to(dtype).pin_memory()
+    vh = torch.randn(pages_host, hkv, P, D, generator=g).to(dtype).pin_memory()
+    return kd, vd, kh, vh
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_append_lands_in_the_named_page(dtype):
+    from directaccesskernel_b200.attention import kv_append_paged
+
+    B, Hkv, P, D = 4, 2, 16, 128
+    kd, vd, kh, vh = _pools(5, 5, Hkv, P, D, dtype)
+    table = torch.tensor([[0, -1, 3], [-2, 1, -5], [4, -3, 2], [-4, -5, 0]], dtype=torch.int32)
+    pos = torch.tensor([20, 2, 40, 10], dtype=torch.int32)  # host, host, device, host
+    g = torch.Generator().manual_seed(1)
+    kn = torch.randn(B, Hkv, D, generator=g).to(dtype)
+    vn = torch.randn(B, Hkv, D, generator=g).to(dtype)
+    exp = [t.cpu().clone() for t in (kd, vd, kh, vh)]
+    for b in range(B):
+        e = int(table[b, pos[b] // P])
+        slot = int(pos[b]) % P
+        if e >= 0:
+            exp[0][e, :, slot] = kn[b]
+            exp[1][e, :, slot] = vn[b]
+        else:
+            exp[2][-1 - e, :, slot] = kn[b]
+            exp[3][-1 - e, :, slot] = vn[b]
+    kv_append_paged(kn.cuda(), vn.cuda(), kd, vd, kh, vh, table.cuda(), pos.cuda())
+    torch.cuda.synchronize()
+    for got, want in zip((kd, vd, kh, vh), exp):
+        assert torch.equal(got.cpu(), want)
+
+
+def test_cache_built_token_by_token_decodes_like_the_oracle():
+    from directaccesskernel_b200 import runtime
+    from directaccesskernel_b200.attention import decode_paged, kv_append_paged
+
+    B, Hq, Hkv, P, D, L = 3, 8, 2, 16, 128, 75
+    npg = (L + P - 1) // P
+    kd, vd, kh, vh = _pools(B * npg, B * npg, Hkv, P, D)
+    # Alternate tiers page by page, differently per sequence.
+    table = torch.empty(B, npg, dtype=torch.int32)
+    for b in range(B):
+        for j in range(npg):
+            table[b, j] = (b * npg + j) if (b + j) % 2 else -1 - (b * npg + j)
+    tab = table.cuda()
+    g = torch.Generator().manual_seed(3)
+    K = torch.randn(B, Hkv, L, D, generator=g).half()
+    V = torch.randn(B, Hkv, L, D, generator=g).half()
+    for t in range(L):
+        pos = torch.full((B,), t, dtype=torch.int32, device="cuda")
+        kv_append_paged(K[:, :, t].contiguous().cuda(), V[:, :, t].contiguous().cuda(), kd, vd, kh, vh, tab, pos)
+    q = torch.randn(B, Hq, D, generator=g).half()
+    seq = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    out = decode_paged(q.cuda(), kd, vd, kh, vh, tab, seq, 1 / math.sqrt(D), 64)
+    ref = oracle.decode_attention(q.numpy()[:, :, None, :], K.numpy(), V.numpy(), None, 1 / math.sqrt(D))[:, 0]
+    assert rel_err(out.float().cpu().numpy(), ref) < 2e-3
+    assert runtime.device_status() == 0
+
+
+def test_bad_entries_are_recorded_not_written():
+    from directaccesskernel_b200 import _lib, runtime
+    from directaccesskernel_b200.attention import kv_append_paged
+
+    Hkv, P = 2, 16
+    kd, vd, kh, vh = _pools(2, 2, Hkv, P)
+    before = [t.cpu().clone() for t in (kd, vd, kh, vh)]
+    table = torch.tensor([[0, 7], [-9, 1]], dtype=torch.int32, device="cuda")  # device page 7, host page 8 do not exist
+    pos = torch.tensor([20, 5], dtype=torch.int32, device="cuda")
+    kn = torch.randn(2, Hkv, 128).half().cuda()
+    assert runtime.device_status() == 0
+    kv_append_paged(kn, kn.clone(), kd, vd, kh, vh, table, pos)
+    assert runtime.device_status(clear=True) == _lib.DAK_ERR_INVALID_ARG
+    for got, want in zip((kd, vd, kh, vh), before):
+        assert torch.equal(got.cpu(), want)
+    # A position past the table is caught too.
+    kv_append_paged(kn, kn.clone(), kd, vd, kh, vh, table, torch.tensor([40, 0], dtype=torch.int32, device="cuda"))
+    assert runtime.device_status(clear=True) == _lib.DAK_ERR_INVALID_ARG
+
+
+def test_append_argument_errors():
+    from directaccesskernel_b200.attention import kv_append_paged
+
+    kd, vd, kh, vh = _pools(2, 2, 2, 16)
+    table = torch.zeros(1, 2, dtype=torch.int32, device="cuda")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kn = torch.randn(1, 2, 128).half().cuda()
+    with pytest.raises(RuntimeError):
+        kv_append_paged(kn, kn, kd, vd, kh.clone(), vh, table, pos)  # unpinned host pool
+    with pytest.raises(RuntimeError):
+        kv_append_paged(kn.float(), kn.float(), kd, vd, kh, vh, table, pos)
+    with pytest.raises(RuntimeError):
+        kv_append_paged(kn, kn, kd, None, kh, vh, table, pos)
