@@ -54,8 +54,16 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["linear", "attention", "opt66b"], default="linear")
-    ap.add_argument("--hbm-budget-gb", type=float, default=96.0, help="opt66b: HBM weight budget (GB)")
+    ap.add_argument("--workload", choices=["linear", "attention", "opt66b", "llama70b"], default="linear")
+    ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
+    ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
+    ap.add_argument("--ctx", type=int, default=16384, help="llama70b: context tokens per sequence")
+    ap.add_argument("--no-balance", action="store_true",
+                    help="llama70b: same host fraction on every rank (default: balanced by host bandwidth)")
+    ap.add_argument("--host-fraction", type=float, default=None,
+                    help="llama70b: fixed host fraction of weights and KV (default: from the HBM budget)")
+    ap.add_argument("--hbm-budget-gb", type=float, default=None,
+                    help="HBM budget in GB (opt66b: weights, default 96; llama70b: per GPU, default 60)")
     ap.add_argument("--prompt-len", type=int, default=512, help="opt66b: prompt tokens")
     ap.add_argument("--tokens", type=str, default=None, help="comma list overriding the M sweep")
     ap.add_argument("--ratios", type=str, default=None, help="comma list overriding the ratio sweep")
@@ -130,15 +138,23 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ link probes
-def host_link_probe(torch, runtime):
-    """Host->GPU read bandwidth: DMA copy of pinned memory and the TMA read probe."""
+def host_link_probe(torch, runtime, world: int = 1):
+    """Host->GPU read bandwidth: DMA copy of pinned memory and the TMA read probe.
+    Under torchrun every rank measures at the same time (barriers between the
+    phases), so the figures include the contention of all GPUs on the host."""
+    def sync():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
+
     n = 1 << 30
     src = torch.empty(n, dtype=torch.uint8).pin_memory()
     src.fill_(1)
     dst = torch.empty(n, dtype=torch.uint8, device="cuda")
     for _ in range(2):
         dst.copy_(src, non_blocking=True)
-    torch.cuda.synchronize()
+    sync()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(3):
@@ -149,7 +165,7 @@ def host_link_probe(torch, runtime):
     best = 0.0
     for ctas in (16, 32, 64):
         runtime.probe_stream_read(src, ctas, 4, 32768)
-        torch.cuda.synchronize()
+        sync()
         e0.record()
         runtime.probe_stream_read(src, ctas, 4, 32768)
         e1.record()
@@ -211,7 +227,7 @@ def run_linear(args, torch, rank, world):
     tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else list(TOKENS)
     ratios = [float(r) for r in args.ratios.split(",")] if args.ratios else list(RATIOS)
     hbm_gbs, peak_kind = measured_peaks()
-    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime)
+    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime, world)
     host_gbs = max(dma_gbs, tma_host_gbs)
     hbm_read_gbs = hbm_read_probe(torch, runtime)
 
@@ -445,7 +461,7 @@ def run_attention(args, torch, rank, world):
     from directaccesskernel_b200.attention import auto_split_size, decode_paged
 
     hbm_gbs, peak_kind = measured_peaks()
-    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime)
+    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime, world)
     host_gbs = max(dma_gbs, tma_host_gbs)
     B, Hq, Hkv, S, P = 8, 32, 8, 32768, 16
     g = torch.Generator(device="cuda").manual_seed(rank)
@@ -573,10 +589,11 @@ def run_opt66b(args, torch, rank, world):
     from directaccesskernel_b200 import decode, runtime
 
     hbm_gbs, peak_kind = measured_peaks()
-    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime)
+    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime, world)
     host_gbs = max(dma_gbs, tma_host_gbs)
     cfg = decode.opt_config("opt-66b")
-    budget = int(args.hbm_budget_gb * 1e9)
+    budget_gb = 96.0 if args.hbm_budget_gb is None else args.hbm_budget_gb
+    budget = int(budget_gb * 1e9)
     t0 = time.perf_counter()
     model, stats = decode.build_offloaded_model(cfg, linear_type="horizontal", hbm_budget_bytes=budget, seed=rank)
     build_s = time.perf_counter() - t0
@@ -620,7 +637,7 @@ def run_opt66b(args, torch, rank, world):
         "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(tbt, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
         "data": "synthetic: random N(0,0.02) weights, random prompt ids",
-        "config": {"workload": f"BASELINE config 4: OPT-66B arch, HBM budget {args.hbm_budget_gb:g} GB, batch {B}, "
+        "config": {"workload": f"BASELINE config 4: OPT-66B arch, HBM budget {budget_gb:g} GB, batch {B}, "
                                f"prompt {L}, greedy decode", "model_bytes": model_bytes,
                    "host_bytes": stats.host_bytes, "device_bytes": stats.device_bytes,
                    "weight_offload_ratio": round(stats.actual_offload_ratio, 4), "build_s": round(build_s, 1),
@@ -640,6 +657,205 @@ def run_opt66b(args, torch, rank, world):
         "gpu_launches": OPT66B_LINEARS_PER_LAYER * n_layers * K, "clocks": clocks.summary(),
         **({"cpu_baseline": cpu} if cpu is not None else {}),
     }
+
+
+def run_llama70b(args, torch, rank, world):
+    """Llama-3-70B architecture, tensor-parallel over the
+    torchrun ranks, batch 32, context 16384 (random KV standing in for the
+    prefill), a per-GPU HBM budget (60 GB) that puts the same fraction of each
+    rank's weights and KV pages in its pinned host memory.  One step = one
+    greedy decode step of all sequences (one CUDA graph, NCCL all-reduce after
+    o and down).  ``--layers`` and ``--host-fraction`` give the reduced-depth,
+    fixed-fraction variant whose host bytes fit the box at every TP size."""
+    import psutil
+
+    from directaccesskernel_b200 import decode, runtime
+    from directaccesskernel_b200.llama_tp import LlamaShape, TPLlamaDecoder, budget_fraction
+
+    hbm_gbs, peak_kind = measured_peaks()
+    dma_gbs, tma_host_gbs = host_link_probe(torch, runtime, world)
+    host_gbs = max(dma_gbs, tma_host_gbs)
+    cfg = decode.llama_config("llama-3-70b", num_hidden_layers=args.layers)
+    shape = LlamaShape.from_config(cfg)
+    B, ctx = args.batch, args.ctx
+    W, K = max(3, args.warmup), args.steps
+    max_ctx = ctx + W + K + 4
+    budget_gb = 60.0 if args.hbm_budget_gb is None else args.hbm_budget_gb
+    frac = (args.host_fraction if args.host_fraction is not None
+            else budget_fraction(shape, world, B, max_ctx, int(budget_gb * 1e9)))
+    per_rank_total = shape.weight_bytes_per_rank(world) + shape.kv_bytes_per_rank(world, B, max_ctx)
+    host_need = frac * per_rank_total * world
+    # The ranks share the box's host-memory bandwidth unevenly; give each rank a
+    # share of the host bytes proportional to its concurrently measured
+    # GPU-initiated read bandwidth, so that all host streams finish together.
+    fracs = [frac] * world
+    if world > 1 and frac > 0 and not args.no_balance:
+        bw = torch.tensor([tma_host_gbs], dtype=torch.float64, device="cuda")
+        allbw = torch.empty(world, dtype=torch.float64, device="cuda")
+        torch.distributed.all_gather_into_tensor(allbw, bw)
+        lo = max(0.0, 1.0 - budget_gb * 1e9 / per_rank_total)
+        fracs = balanced_host_fractions(frac, allbw.tolist(), lo)
+    my_frac = fracs[rank]
+    ram = psutil.virtual_memory().total
+    if host_need > 0.75 * ram:
+        raise SystemExit(f"llama70b at TP{world}: {host_need / 1e9:.0f} GB of pinned host memory needed, more than "
+                         f"3/4 of the box's {ram / 1e9:.0f} GB; use --layers / --host-fraction")
+    t0 = time.perf_counter()
+    dec = TPLlamaDecoder(shape, batch=B, max_ctx=max_ctx, weight_offload=my_frac, kv_host_fraction=my_frac)
+    dec.init_random(seed=0)
+    dec.fill_kv_random(ctx, seed=1)
+    g = torch.Generator().manual_seed(3)
+    dec.ids.copy_(torch.randint(0, shape.vocab, (B,), generator=g).cuda())
+    build_s = time.perf_counter() - t0
+    dec.capture()
+    for _ in range(W):
+        dec.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        e0.record()
+        for _ in range(K):
+            dec.step()
+        e1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1)
+    # End to end: every step the new tokens go to pinned host memory and the host
+    # waits for them, as a serving loop that streams tokens out does.
+    tok_host = torch.empty(B, dtype=torch.long).pin_memory()
+    torch.cuda.synchronize()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        dec.step()
+        tok_host.copy_(dec.ids, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e2)
+    status = runtime.device_status()
+    times = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms = times.tolist()
+    dec.release()
+    if status != 0:
+        raise RuntimeError(f"device error word {status} after the timed region")
+
+    # Bytes one step reads on this rank: every linear weight once, every KV page of
+    # the context once (plus the new token's pages); x/y and norms are negligible.
+    lin_host = sum(p.numel() * p.element_size() for m in dec.modules() for p in m.parameters(recurse=False)
+                   if p.device.type == "cpu")
+    lin_dev = sum(p.numel() * p.element_size() for l in dec.layers for p in l.parameters() if p.device.type == "cuda")
+    lin_dev += sum(p.numel() * p.element_size() for p in dec.lm_head.parameters() if p.device.type == "cuda")
+    kv_host, kv_dev = dec.kv_bytes()
+    fill = min(1.0, (ctx + 1) / max_ctx)
+    host_step, dev_step = lin_host + kv_host * fill, lin_dev + kv_dev * fill
+    roof_ms = max(dev_step / (hbm_gbs * 1e9), host_step / (host_gbs * 1e9)) * 1e3
+    # Whole-job figures: the slowest rank's lower bound, summed bytes, the
+    # lowest host link.
+    agg = torch.tensor([roof_ms, host_step, dev_step, -host_gbs], dtype=torch.float64, device="cuda")
+    if world > 1:
+        mx = agg[[0, 3]].clone()
+        sm = agg[[1, 2]].clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(sm)
+        roof_ms, host_gbs = mx[0].item(), -mx[1].item()
+        host_step, dev_step = sm[0].item() / world, sm[1].item() / world
+    step_ms = ms / K
+    launches_per_step = shape.layers * 6 + 1  # 4 linears, KV append, attention (+ merge) per layer; lm_head
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_llama70b(B, ctx, shape.layers)
+    return {
+        "metric": "decode tokens/s (Llama-3-70B arch, tensor parallel, weights and KV offloaded)",
+        "value": round(B * K / (ms * 1e-3), 3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(step_ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate / softmax)",
+        "data": "synthetic: random N(0,0.02) weights, N(0,1) KV for the context, random token ids",
+        "config": {"workload": f"BASELINE config 5: Llama-3-70B arch, {shape.layers} layers, batch {B}, ctx {ctx}, "
+                               f"TP{world}, per-GPU HBM budget {budget_gb:g} GB"
+                               + ("" if args.host_fraction is None else f", fixed host fraction {frac:g}"),
+                   "host_fraction": round(frac, 4), "per_rank_host_fractions": [round(f, 4) for f in fracs],
+                   "rank0_host_bytes": int(lin_host + kv_host),
+                   "rank0_device_bytes": int(lin_dev + kv_dev), "build_s": round(build_s, 1),
+                   "parallelism": f"tp{world}", "l2": "tens of GB read per step exceed L2",
+                   "timing": "CUDA events around K graph replays, max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": round((host_step + dev_step) / (step_ms * 1e-3) / 1e9, 2),
+                     "peak": round((host_step + dev_step) / (roof_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                     "frac": round(roof_ms / step_ms, 4),
+                     "traffic": round(dev_step * DRAM_PER_DEVICE_BYTE),
+                     "traffic_basis": "per rank per step: device-resident weight and KV bytes x the DRAM/device-byte "
+                                      "ratio of the linear captures",
+                     "peak_model": "slowest rank's max(device bytes / HBM, host bytes / its host link) per step; "
+                                   "achieved and peak are per-rank averages of the bytes",
+                     "hbm_gbs": hbm_gbs, "hbm_peak_kind": peak_kind, "host_link_gbs_min": round(host_gbs, 2)},
+        "e2e": {"value": round(B * K / (e2e_ms * 1e-3), 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 8 * B},
+        "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
+        **({"cpu_baseline": cpu} if cpu is not None else {}),
+    }
+
+
+def balanced_host_fractions(mean_frac: float, bandwidths: list[float], lo: float = 0.0) -> list[float]:
+    """Per-rank host fractions whose mean is ``mean_frac`` and which are proportional
+    to the ranks' host bandwidths, clamped to [lo, 1] (lo keeps the device part
+    within the HBM budget); clamped ranks hand their excess to the others."""
+    n = len(bandwidths)
+    fr = [mean_frac] * n
+    free = list(range(n))
+    total = mean_frac * n
+    for _ in range(n):
+        bw = sum(bandwidths[i] for i in free)
+        fixed = sum(fr[i] for i in range(n) if i not in free)
+        for i in free:
+            fr[i] = (total - fixed) * bandwidths[i] / bw
+        out = [i for i in free if fr[i] > 1.0 or fr[i] < lo]
+        if not out:
+            break
+        for i in out:
+            fr[i] = min(1.0, max(lo, fr[i]))
+            free.remove(i)
+        if not free:
+            break
+    return fr
+
+
+def cpu_baseline_llama70b(batch: int = 32, ctx: int = 16384, layers: int = 80):
+    """The oracle port on the host cores for one config-5 decode step: numpy FP32
+    of one Llama-3-70B layer's linears at batch 32 and of one sequence's GQA
+    attention over its 16384-token context, extrapolated to 32 sequences and 80
+    layers (the CPU cannot hold the model; labelled extrapolated)."""
+    import numpy as np
+
+    import oracle
+    import oracle.attention as oatt
+
+    h, f, hq, hkv, d = 8192, 28672, 64, 8, 128
+    rng = np.random.default_rng(0)
+    shapes = [(hq * d, h), (hkv * d, h), (hkv * d, h), (h, hq * d), (f, h), (f, h), (h, f)]
+    t_lin = 0.0
+    for shp in shapes:
+        w = rng.standard_normal(shp, dtype=np.float32) * np.float32(0.02)
+        x = rng.standard_normal((batch, shp[1]), dtype=np.float32)
+        t = time.perf_counter()
+        oracle.linear(x, w, acc=np.float32)
+        t_lin += time.perf_counter() - t
+        del w
+    k = rng.standard_normal((1, hkv, ctx, d), dtype=np.float32)
+    v = rng.standard_normal((1, hkv, ctx, d), dtype=np.float32)
+    q = rng.standard_normal((1, hq, 1, d), dtype=np.float32)
+    t = time.perf_counter()
+    oatt.decode_attention_grouped(q, k, v, 1.0 / math.sqrt(d))
+    t_att = time.perf_counter() - t
+    t_step = layers * (t_lin + batch * t_att)
+    return {"value": round(batch / t_step, 5), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one Llama-3-70B layer's 7 linears at batch {batch} + one sequence's attention over "
+                      f"{ctx} tokens (numpy FP32), extrapolated to {batch} sequences x {layers} layers (extrapolated)"}
 
 
 def cpu_baseline_opt66b(reps: int = 2):
@@ -676,12 +892,16 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    if args.workload in ("attention", "opt66b"):
-        fn = cpu_baseline_attention if args.workload == "attention" else cpu_baseline_opt66b
-        metric, unit = (("split-KV decode attention KV GB/s", "GB/s") if args.workload == "attention" else
-                        ("decode tokens/s (OPT-66B arch, HBM weight budget)", "tokens/s"))
+    if args.workload in ("attention", "opt66b", "llama70b"):
+        fn = {"attention": cpu_baseline_attention, "opt66b": cpu_baseline_opt66b,
+              "llama70b": lambda: cpu_baseline_llama70b(args.batch, args.ctx, args.layers)}[args.workload]
+        metric, unit = {
+            "attention": ("split-KV decode attention KV GB/s", "GB/s"),
+            "opt66b": ("decode tokens/s (OPT-66B arch, HBM weight budget)", "tokens/s"),
+            "llama70b": ("decode tokens/s (Llama-3-70B arch, tensor parallel, weights and KV offloaded)", "tokens/s"),
+        }[args.workload]
         for _ in range(max(0, min(args.warmup, 1))):
-            fn() if args.workload == "opt66b" else fn(budget_s=2.0)
+            fn(budget_s=2.0) if args.workload == "attention" else fn()
         t0 = time.perf_counter()
         runs = [fn() for _ in range(args.steps)]
         elapsed = time.perf_counter() - t0
@@ -691,8 +911,8 @@ def run_reference(args):
             "metric": metric, "impl": "reference", "value": v, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed / max(1, args.steps) * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": f"BASELINE {'config 3' if args.workload == 'attention' else 'config 4'} "
-                                   "sample on host cores"},
+            "config": {"workload": "BASELINE " + {"attention": "config 3", "opt66b": "config 4",
+                                                  "llama70b": "config 5"}[args.workload] + " sample on host cores"},
             "cpu_baseline": cpu,
             "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
@@ -736,7 +956,7 @@ def main():
 
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     try:
-        fn = {"attention": run_attention, "opt66b": run_opt66b}.get(args.workload, run_linear)
+        fn = {"attention": run_attention, "opt66b": run_opt66b, "llama70b": run_llama70b}.get(args.workload, run_linear)
         line = fn(args, torch, rank, world)
         if rank == 0:
             print(json.dumps(line), flush=True)
