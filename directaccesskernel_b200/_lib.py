@@ -119,6 +119,9 @@ SIGNATURES = {
     "dak_attn_decode": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_attn_decode_paged": (c_int, [ctypes.POINTER(AttnPagedArgs), c_vp]),
     "dak_kv_append_paged": (c_int, [ctypes.POINTER(KvAppendArgs), c_vp]),
+    "dak_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_i64, ctypes.c_float, c_int, c_vp]),
+    "dak_rope_qk": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp]),
+    "dak_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_int, c_int, c_int, c_vp]),
     "dak_attn_decode_noalloc": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_device_status": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "dak_selftest_wait_timeout": (c_int, [ctypes.c_uint, c_vp]),

@@ -1,0 +1,183 @@
+// dak_decode_ops.cu - the element-wise steps of a Llama decode layer around the
+// offloaded linears and the decode attention: RMSNorm (with the residual add
+// fused in), rotary embedding of q and k, and the SiLU-gated product.
+//
+// The reference runs these as separate torch ops inside its vendored model
+// (app/python/llama/vanila_llama.py:227-400, from transformers' Llama); one
+// decode layer then costs ~35 tiny launches besides the linears.  Each kernel
+// here follows those ops' arithmetic, including the roundings to 16 bit
+// between them, so results match transformers to within FP32 reduction order.
+#include <algorithm>
+#include <cstring>
+
+#include "dak_common.cuh"
+#include "dak_host.h"
+
+namespace dak {
+namespace {
+
+template <typename T> __device__ __forceinline__ float ld1(const void *p, long long i) {
+  return Elem<T>::to_float(reinterpret_cast<const uint16_t *>(p)[i]);
+}
+template <typename T> __device__ __forceinline__ void st1(void *p, long long i, float v) {
+  reinterpret_cast<uint16_t *>(p)[i] = Elem<T>::from_float(v);
+}
+// Rounds through the 16-bit type, as a torch op on 16-bit tensors does.
+template <typename T> __device__ __forceinline__ float r16(float v) {
+  return Elem<T>::to_float(Elem<T>::from_float(v));
+}
+
+constexpr int kNormThreads = 256;
+
+// One CTA per row.  h = x (+ residual, rounded to 16 bit); out = w * round16(h *
+// rsqrt(mean(h^2) + eps)) with the statistics in FP32 (transformers LlamaRMSNorm).
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const void *x, const void *res, const void *w, void *out,
+                                                               void *res_out, int cols, long long ld, float eps) {
+  const long long row = blockIdx.x;
+  const void *xr = static_cast<const uint16_t *>(x) + row * ld;
+  const void *rr = res ? static_cast<const uint16_t *>(res) + row * ld : nullptr;
+  void *ro = res_out ? static_cast<void *>(static_cast<uint16_t *>(res_out) + row * ld) : nullptr;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < cols; c += kNormThreads) {
+    float h = ld1<T>(xr, c);
+    if (rr) h = r16<T>(h + ld1<T>(rr, c));
+    if (ro) st1<T>(ro, c, h);
+    ss = fmaf(h, h, ss);
+  }
+  __shared__ float red[kNormThreads / 32];
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / (float)cols + eps);
+  void *orow = static_cast<uint16_t *>(out) + row * (long long)cols;
+  for (int c = threadIdx.x; c < cols; c += kNormThreads) {
+    // Re-read h: from res_out when the add was fused (it may alias x or res).
+    float h = ro ? ld1<T>(ro, c) : ld1<T>(xr, c);
+    st1<T>(orow, c, ld1<T>(w, c) * r16<T>(h * inv));
+  }
+}
+
+// One CTA per (sequence, head) of q, k and v, head_dim / 2 threads: for q and k,
+// thread i rotates the pair (i, i + d/2) with cos/sin of position * inv_freq[i]
+// rounded to 16 bit (transformers apply_rotary_pos_emb, default rotary
+// embedding); v heads are copied, so all three outputs are contiguous.
+template <typename T>
+__global__ void rope_qk_kernel(const void *qkv, long long ld, const int32_t *pos, const float *inv_freq, void *q_out,
+                               void *k_out, void *v_out, int q_heads, int kv_heads, int d) {
+  const int heads = q_heads + 2 * kv_heads;
+  const int b = blockIdx.x / heads;
+  const int hh = blockIdx.x - b * heads;
+  const int i = threadIdx.x;
+  const int half = d / 2;
+  if (i >= half) return;
+  const long long src = (long long)b * ld + (long long)hh * d;
+  const uint16_t *in = reinterpret_cast<const uint16_t *>(qkv);
+  if (hh >= q_heads + kv_heads) {
+    uint16_t *vo = reinterpret_cast<uint16_t *>(v_out) + ((long long)b * kv_heads + (hh - q_heads - kv_heads)) * d;
+    vo[i] = in[src + i];
+    vo[i + half] = in[src + i + half];
+    return;
+  }
+  const float f = (float)pos[b] * inv_freq[i];
+  const float c = r16<T>(cosf(f)), s = r16<T>(sinf(f));
+  const float x1 = ld1<T>(qkv, src + i), x2 = ld1<T>(qkv, src + i + half);
+  // out[i] = x1*c + (-x2)*s ; out[i + d/2] = x2*c + x1*s, each product and sum rounded.
+  const float o1 = r16<T>(r16<T>(x1 * c) + r16<T>(-x2 * s));
+  const float o2 = r16<T>(r16<T>(x2 * c) + r16<T>(x1 * s));
+  void *dst;
+  long long off;
+  if (hh < q_heads) {
+    dst = q_out;
+    off = ((long long)b * q_heads + hh) * d;
+  } else {
+    dst = k_out;
+    off = ((long long)b * kv_heads + (hh - q_heads)) * d;
+  }
+  st1<T>(dst, off + i, o1);
+  st1<T>(dst, off + i + half, o2);
+}
+
+// out[r, c] = round16(silu(g)) * u with g = gu[r, c], u = gu[r, cols + c].
+template <typename T>
+__global__ void silu_mul_kernel(const void *gu, long long ld, void *out, int rows, int cols) {
+  const long long n = (long long)rows * cols;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const long long r = e / cols;
+    const int c = (int)(e - r * cols);
+    const float g = ld1<T>(gu, r * ld + c);
+    const float u = ld1<T>(gu, r * ld + cols + c);
+    const float sg = r16<T>(g / (1.0f + expf(-g)));
+    st1<T>(out, e, sg * u);
+  }
+}
+
+int check_dtype(int dtype) {
+  if (dtype != DAK_DTYPE_F16 && dtype != DAK_DTYPE_BF16)
+    return fail(DAK_ERR_UNSUPPORTED, "decode ops support float16 and bfloat16");
+  return DAK_OK;
+}
+
+}  // namespace
+}  // namespace dak
+
+extern "C" int dak_rmsnorm(const void *x, const void *residual, const void *weight, void *out, void *residual_out,
+                           int rows, int cols, int64_t ld, float eps, int dtype, void *stream) {
+  using namespace dak;
+  int st = check_dtype(dtype);
+  if (st) return st;
+  if (!x || !weight || !out || rows <= 0 || cols <= 0 || ld < cols)
+    return fail(DAK_ERR_INVALID_ARG, "rmsnorm: x, weight, out and rows, cols > 0, ld >= cols are required");
+  if ((residual == nullptr) != (residual_out == nullptr))
+    return fail(DAK_ERR_INVALID_ARG, "rmsnorm: residual and residual_out come together");
+  auto s = static_cast<cudaStream_t>(stream);
+  if (dtype == DAK_DTYPE_F16)
+    rmsnorm_kernel<__half><<<rows, kNormThreads, 0, s>>>(x, residual, weight, out, residual_out, cols, ld, eps);
+  else
+    rmsnorm_kernel<__nv_bfloat16><<<rows, kNormThreads, 0, s>>>(x, residual, weight, out, residual_out, cols, ld, eps);
+  return cuda_status(cudaGetLastError(), "rmsnorm launch");
+}
+
+extern "C" int dak_rope_qk(const void *qkv, int64_t ld, const int32_t *positions, const float *inv_freq, void *q_out,
+                           void *k_out, void *v_out, int batch, int q_heads, int kv_heads, int head_dim, int dtype,
+                           void *stream) {
+  using namespace dak;
+  int st = check_dtype(dtype);
+  if (st) return st;
+  if (!qkv || !positions || !inv_freq || !q_out || !k_out || !v_out || batch <= 0 || q_heads <= 0 || kv_heads <= 0)
+    return fail(DAK_ERR_INVALID_ARG, "rope_qk: all buffers and positive sizes are required");
+  if (head_dim <= 0 || head_dim % 2 || head_dim > 1024)
+    return fail(DAK_ERR_INVALID_ARG, "rope_qk: head_dim must be even and at most 1024");
+  if (ld < (int64_t)(q_heads + 2 * kv_heads) * head_dim)
+    return fail(DAK_ERR_INVALID_ARG, "rope_qk: qkv row stride below (q_heads + 2 kv_heads) x head_dim");
+  auto s = static_cast<cudaStream_t>(stream);
+  const int grid = batch * (q_heads + 2 * kv_heads);
+  const int threads = ((head_dim / 2 + 31) / 32) * 32;
+  if (dtype == DAK_DTYPE_F16)
+    rope_qk_kernel<__half><<<grid, threads, 0, s>>>(qkv, ld, positions, inv_freq, q_out, k_out, v_out, q_heads,
+                                                    kv_heads, head_dim);
+  else
+    rope_qk_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(qkv, ld, positions, inv_freq, q_out, k_out, v_out,
+                                                           q_heads, kv_heads, head_dim);
+  return cuda_status(cudaGetLastError(), "rope_qk launch");
+}
+
+extern "C" int dak_silu_mul(const void *gate_up, int64_t ld, void *out, int rows, int cols, int dtype, void *stream) {
+  using namespace dak;
+  int st = check_dtype(dtype);
+  if (st) return st;
+  if (!gate_up || !out || rows <= 0 || cols <= 0 || ld < 2 * (int64_t)cols)
+    return fail(DAK_ERR_INVALID_ARG, "silu_mul: buffers, rows, cols > 0 and ld >= 2 cols are required");
+  auto s = static_cast<cudaStream_t>(stream);
+  const long long n = (long long)rows * cols;
+  const int grid = (int)std::min<long long>((n + 255) / 256, 148 * 8);
+  if (dtype == DAK_DTYPE_F16)
+    silu_mul_kernel<__half><<<grid, 256, 0, s>>>(gate_up, ld, out, rows, cols);
+  else
+    silu_mul_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(gate_up, ld, out, rows, cols);
+  return cuda_status(cudaGetLastError(), "silu_mul launch");
+}

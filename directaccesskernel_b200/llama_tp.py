@@ -18,7 +18,8 @@ launch.  A decode step, greedy pick included, is one CUDA graph.
 
 The layer arithmetic follows transformers' Llama (RMSNorm in FP32, rotary
 embedding in the activation dtype, SiLU-gated MLP), which is also what the
-reference's vanila_llama.py runs (app/python/llama/vanila_llama.py:227-400).
+reference's vanila_llama.py runs (app/python/llama/vanila_llama.py:227-400);
+the element-wise steps are the fused kernels of ``decode_ops``.
 """
 from __future__ import annotations
 
@@ -75,18 +76,6 @@ def budget_fraction(shape: LlamaShape, world: int, batch: int, ctx: int, hbm_bud
     + KV) fits the per-GPU HBM budget (0 when everything fits)."""
     total = shape.weight_bytes_per_rank(world) + shape.kv_bytes_per_rank(world, batch, ctx)
     return max(0.0, 1.0 - hbm_budget_bytes / total)
-
-
-def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """transformers LlamaRMSNorm: FP32 statistics, cast back, then scale."""
-    xf = x.float()
-    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return w * xf.to(x.dtype)
-
-
-def _rotate_half(x: torch.Tensor) -> torch.Tensor:
-    h = x.shape[-1] // 2
-    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
 
 
 class _Layer(nn.Module):
@@ -264,6 +253,13 @@ class TPLlamaDecoder(nn.Module):
         self.inv_freq = 1.0 / (self.s.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float32, device=self.device) / d))
         self.next_ids = torch.zeros(B, dtype=torch.long, device=self.device)
         self.logits_full = None
+        h = self.s.hidden
+        self.hidden = torch.empty(B, h, dtype=self.dtype, device=self.device)  # running residual stream
+        self.x_buf = torch.empty(B, h, dtype=self.dtype, device=self.device)
+        self.q_buf = torch.empty(B, self.hq, d, dtype=self.dtype, device=self.device)
+        self.k_buf = torch.empty(B, self.hkv, d, dtype=self.dtype, device=self.device)
+        self.v_buf = torch.empty(B, self.hkv, d, dtype=self.dtype, device=self.device)
+        self.act_buf = torch.empty(B, self.ffn_r, dtype=self.dtype, device=self.device)
 
     def set_positions(self, pos: int) -> None:
         self.pos.fill_(pos)
@@ -274,39 +270,34 @@ class TPLlamaDecoder(nn.Module):
 
     def forward_step(self, keep_logits: bool = False) -> torch.Tensor:
         """One decode step on the static buffers: embeds ``ids`` at ``pos``, writes
-        their K/V, and leaves the greedy tokens in ``next_ids``; advances nothing."""
+        their K/V, and leaves the greedy tokens in ``next_ids``; advances nothing.
+        Per layer: RMSNorm (residual add fused), qkv, rotary, KV append, attention,
+        o + all-reduce, RMSNorm, gate_up, SiLU-gate, down + all-reduce."""
+        from .decode_ops import rmsnorm, rope_qk, silu_mul
+
         s, B, d = self.s, self.B, self.s.head_dim
         torch.add(self.pos, 1, out=self.seq_lens)
-        freqs = self.pos.float()[:, None] * self.inv_freq[None, :]
-        emb = torch.cat((freqs, freqs), dim=-1)
-        cos, sin = emb.cos().to(self.dtype)[:, None, :], emb.sin().to(self.dtype)[:, None, :]
-        h = self.embed[self.ids]
-        qd, kd = self.hq * d, self.hkv * d
+        self.hidden.copy_(self.embed[self.ids])
+        qd = self.hq * d
         scale = 1.0 / math.sqrt(d)
+        x = rmsnorm(self.hidden, self.layers[0].in_w, s.eps, out=self.x_buf)
         for l, layer in enumerate(self.layers):
-            x = _rmsnorm(h, layer.in_w, s.eps)
             qkv = layer.qkv(x)
-            q = qkv[:, :qd].view(B, self.hq, d)
-            k = qkv[:, qd:qd + kd].view(B, self.hkv, d)
-            v = qkv[:, qd + kd:].view(B, self.hkv, d)
-            q = (q * cos + _rotate_half(q) * sin).contiguous()
-            k = (k * cos + _rotate_half(k) * sin).contiguous()
+            rope_qk(qkv, self.pos, self.inv_freq, self.hq, self.hkv, d, self.q_buf, self.k_buf, self.v_buf)
             kdev, vdev, khost, vhost = self._pools(l)
-            kv_append_paged(k, v.contiguous(), kdev, vdev, khost, vhost, self.block_table, self.pos)
-            decode_paged(q, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale, self.split,
+            kv_append_paged(self.k_buf, self.v_buf, kdev, vdev, khost, vhost, self.block_table, self.pos)
+            decode_paged(self.q_buf, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale, self.split,
                          out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
                          max_seq_len=self.max_ctx)
             o = layer.o(self.attn_out.view(B, qd))
             self._all_reduce(o)
-            h = h + o
-            x = _rmsnorm(h, layer.post_w, s.eps)
+            x = rmsnorm(o, layer.post_w, s.eps, residual=self.hidden, out=self.x_buf)
             gu = layer.gate_up(x)
-            a = nn.functional.silu(gu[:, :self.ffn_r]) * gu[:, self.ffn_r:]
-            dn = layer.down(a)
+            dn = layer.down(silu_mul(gu, out=self.act_buf))
             self._all_reduce(dn)
-            h = h + dn
-        h = _rmsnorm(h, self.final_w, s.eps)
-        logits = self.lm_head(h)[:, :max(1, self.vocab_valid)]
+            nxt_w = self.layers[l + 1].in_w if l + 1 < len(self.layers) else self.final_w
+            x = rmsnorm(dn, nxt_w, s.eps, residual=self.hidden, out=self.x_buf)
+        logits = self.lm_head(x)[:, :max(1, self.vocab_valid)]
         val, idx = logits.float().max(dim=-1)
         if self.world > 1:
             pair = torch.stack([val, (idx + self.rank * self.vocab_r).float()], dim=-1)  # [B, 2]

@@ -287,6 +287,33 @@ typedef struct dak_kv_append_args {
 } dak_kv_append_args;
 DAK_API int dak_kv_append_paged(const dak_kv_append_args *args, void *stream);
 
+/* --------------------------------------------------- decode-layer helpers */
+/* The element-wise steps of a Llama decode layer around the linears and the
+ * attention.  No reference counterpart as kernels: the reference runs them as
+ * torch ops in its vendored model (app/python/llama/vanila_llama.py:227-400);
+ * these follow transformers' arithmetic op by op, roundings to 16 bit
+ * included.  Stream-ordered, no allocation. */
+
+/* out[r] = weight * round16(h * rsqrt(mean(h^2) + eps)), statistics in FP32, with
+ * h = x[r] or, when residual is given, h = round16(x[r] + residual[r]), which is
+ * also written to residual_out[r] (may alias x or residual).  x, residual and
+ * residual_out share the row stride ld; out is [rows, cols] contiguous. */
+DAK_API int dak_rmsnorm(const void *x, const void *residual, const void *weight, void *out, void *residual_out,
+                        int rows, int cols, int64_t ld, float eps, int dtype, void *stream);
+
+/* Rotary embedding (default rotary, rotate-half form) of the q and k heads of a
+ * fused qkv row [q_heads | kv_heads | kv_heads] x head_dim with row stride ld:
+ * angle = positions[b] * inv_freq[i] in FP32, cos/sin rounded to 16 bit; writes
+ * q_out [batch, q_heads, head_dim], k_out and v_out [batch, kv_heads, head_dim]
+ * (v copied unchanged). */
+DAK_API int dak_rope_qk(const void *qkv, int64_t ld, const int32_t *positions, const float *inv_freq, void *q_out,
+                        void *k_out, void *v_out, int batch, int q_heads, int kv_heads, int head_dim, int dtype,
+                        void *stream);
+
+/* out[r, c] = round16(silu(gate_up[r, c])) * gate_up[r, cols + c]; gate_up has
+ * row stride ld (>= 2 cols), out is [rows, cols] contiguous. */
+DAK_API int dak_silu_mul(const void *gate_up, int64_t ld, void *out, int rows, int cols, int dtype, void *stream);
+
 /* ------------------------------------------------------------ diagnostics */
 /* Reads (and with clear != 0 resets) the device-side error word that kernels
  * set when a bounded wait times out.  Synchronizes the current device. */
