@@ -187,12 +187,24 @@ def uses_tma() -> bool:
 
 
 def auto_split_size(batch: int, kv_heads: int, max_seq_len: int, num_sms: int | None = None) -> int:
-    """Tokens per split so that batch x kv_heads x splits covers about four waves of CTAs."""
+    """Tokens per split (a multiple of 64) for batch x kv_heads x splits CTAs of one
+    per SM: the split that minimises waves x (64-token chunks per CTA + 2), the
+    2 standing for a CTA's start-up (barrier set-up, first copies in flight).
+    This keeps the last wave full instead of leaving it nearly empty."""
     if num_sms is None:
         from .runtime import NUM_SMS as num_sms
-    want = max(1, (4 * num_sms + batch * kv_heads - 1) // (batch * kv_heads))
-    per = max(64, math.ceil(max_seq_len / want / 64) * 64)
-    return per
+    rows = max(1, batch * kv_heads)
+    chunks_total = max(1, math.ceil(max_seq_len / 64))
+    best, best_cost = 64 * chunks_total, None
+    for chunks in range(1, chunks_total + 1):
+        splits = math.ceil(chunks_total / chunks)
+        if chunks > 1 and math.ceil(chunks_total / (chunks - 1)) == splits:
+            continue  # same split count with fewer chunks per CTA
+        waves = math.ceil(rows * splits / num_sms)
+        cost = waves * (chunks + 2)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = 64 * chunks, cost
+    return best
 
 
 def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_dev: torch.Tensor | None,

@@ -33,6 +33,7 @@ constexpr int kAttnStages = 4;
 constexpr int kAttnComputeWarps = 4;
 constexpr int kAttnThreads = (kAttnComputeWarps + 1) * 32;
 constexpr int kMaxGroup = 8;
+constexpr int kTabWindow = 256;     // block-table entries the producer caches in shared memory
 constexpr uint32_t kHalfBox = kChunk * 128;              // 64 tokens x 64 dims x 2 B = 8 KB
 constexpr uint32_t kKvChunkBytes = 2 * kHalfBox;        // 16 KB for K (or V)
 constexpr uint32_t kStageBytes = 2 * kKvChunkBytes;     // K + V = 32 KB
@@ -63,7 +64,8 @@ struct AttnSmem {
   static constexpr uint32_t redmax_off = p_off + kChunk * kMaxGroup * 4;      // 2 x 4 x G
   static constexpr uint32_t ored_off = redmax_off + 2 * kAttnComputeWarps * kMaxGroup * 4;  // 4 x G x 128
   static constexpr uint32_t lred_off = ored_off + kAttnComputeWarps * kMaxGroup * kHeadDim * 4;
-  static constexpr uint32_t bar_off = lred_off + kAttnComputeWarps * kMaxGroup * 4;
+  static constexpr uint32_t tab_off = lred_off + kAttnComputeWarps * kMaxGroup * 4;  // block-table window
+  static constexpr uint32_t bar_off = tab_off + kTabWindow * 4;
   static constexpr uint32_t flag_off = bar_off + 2 * kAttnStages * 8;
   static constexpr uint32_t bytes = flag_off + 16 + 1024;
 };
@@ -76,6 +78,36 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(policy)
       : "memory");
 }
+
+// Four 8x8 16-bit matrices from shared memory (row addresses from lanes 8j..8j+7
+// for matrix j), optionally transposed; the operand loads of mma.sync.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+// D = A (16x16, row) * B (16x8, col) + D with 16-bit inputs and FP32 accumulators.
+template <typename T> struct Mma;
+template <> struct Mma<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+template <> struct Mma<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
 
 // Where page j (page_size tokens) of sequence b lives: tier (0 host, 1 device),
 // the row offset inside the tile map's second dimension and the slab index
@@ -117,8 +149,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
   const int t_end = min(seq, t_begin + p.split_size);
   const int nchunks = t_end > t_begin ? (t_end - t_begin + kChunk - 1) / kChunk : 0;
 
-  float *q_s = reinterpret_cast<float *>(smem + S::q_off);
-  float *p_s = reinterpret_cast<float *>(smem + S::p_off);
   float *redmax = reinterpret_cast<float *>(smem + S::redmax_off);
   float *ored = reinterpret_cast<float *>(smem + S::ored_off);
   float *lred = reinterpret_cast<float *>(smem + S::lred_off);
@@ -135,48 +165,70 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
     *abort_flag = 0;
     fence_mbar_init();
   }
-  // Query heads kvh*G .. kvh*G+G-1 (repeat_kv order) into shared memory as FP32.
-  for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x) {
-    const int g = i / kHeadDim, d = i % kHeadDim;
-    const uint16_t *q = reinterpret_cast<const uint16_t *>(p.query) + (long long)b * p.q_stride_b +
-                        (long long)(kvh * G + g) * p.q_stride_h;
-    q_s[g * kHeadDim + d] = Elem<T>::to_float(q[d]);
-  }
   __syncthreads();
 
   if (warp == kAttnComputeWarps) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && nchunks > 0) {
-      for (int t = 0; t < 2; ++t) {
-        prefetch_tensormap(&p.kmap[t]);
-        prefetch_tensormap(&p.vmap[t]);
-      }
+    // Lane 0 issues the copies.  In paged mode the whole warp first loads a
+    // window of the split's block-table entries into shared memory with one
+    // coalesced pass, so no copy waits on a dependent global load.
+    if (nchunks > 0) {
+      if (lane == 0)
+        for (int t = 0; t < 2; ++t) {
+          prefetch_tensormap(&p.kmap[t]);
+          prefetch_tensormap(&p.vmap[t]);
+        }
       const uint64_t pol = l2_policy_evict_first();
       const int psz = p.block_table ? p.page_size : kChunk;
+      int *tab_s = reinterpret_cast<int *>(smem + S::tab_off);
+      const int seq_pages = (t_end + psz - 1) / psz;  // table entries this split may read
+      int win = -kTabWindow;                          // first page held in tab_s
       uint32_t issued_mask = 0, issued_par = 0;
       for (int c = 0; c < nchunks; ++c) {
         const int s = c % kAttnStages;
         const uint32_t ph = (uint32_t)((c / kAttnStages) & 1);
-        if (!mbar_wait<false>(empty0 + 8 * s, ph ^ 1u, wc)) break;
         const int c0 = t_begin + c * kChunk;
         const int valid = min(kChunk, t_end - c0);
         const int npages = (valid + psz - 1) / psz;
-        const uint32_t fb = full0 + 8 * s;
-        mbar_arrive_expect_tx(fb, (uint32_t)npages * (uint32_t)psz * 128u * 4u);
-        const uint32_t kdst = sbase + S::kv_off + s * kStageBytes;
-        const uint32_t vdst = kdst + kKvChunkBytes;
-        for (int pg = 0; pg < npages; ++pg) {
-          const PageLoc loc = locate(p, b, c0 + pg * psz);
-          const uint32_t row_off = (uint32_t)(pg * psz) * 128u;
-          for (int h = 0; h < 2; ++h) {
-            tma_load_4d(kdst + h * kHalfBox + row_off, &p.kmap[loc.tier], h * 64, loc.row, kvh, loc.slab, fb, pol);
-            tma_load_4d(vdst + h * kHalfBox + row_off, &p.vmap[loc.tier], h * 64, loc.row, kvh, loc.slab, fb, pol);
+        const int pfirst = c0 / psz;
+        if (p.block_table && pfirst + npages > win + kTabWindow) {
+          win = pfirst;
+          __syncwarp();
+          for (int i = lane; i < kTabWindow && win + i < seq_pages; i += 32)
+            tab_s[i] = p.block_table[(long long)b * p.bt_stride + win + i];
+          __syncwarp();
+        }
+        int ok = 1;
+        if (lane == 0) {
+          ok = mbar_wait<false>(empty0 + 8 * s, ph ^ 1u, wc) ? 1 : 0;
+          if (ok) {
+            const uint32_t fb = full0 + 8 * s;
+            mbar_arrive_expect_tx(fb, (uint32_t)npages * (uint32_t)psz * 128u * 4u);
+            const uint32_t kdst = sbase + S::kv_off + s * kStageBytes;
+            const uint32_t vdst = kdst + kKvChunkBytes;
+            for (int pg = 0; pg < npages; ++pg) {
+              PageLoc loc;
+              if (p.block_table) {
+                const int v = tab_s[pfirst + pg - win];
+                loc.tier = v < 0 ? 0 : 1;
+                loc.slab = v < 0 ? (-1 - v) : v;
+                loc.row = 0;
+              } else {
+                loc = locate(p, b, c0 + pg * psz);
+              }
+              const uint32_t row_off = (uint32_t)(pg * psz) * 128u;
+              for (int h = 0; h < 2; ++h) {
+                tma_load_4d(kdst + h * kHalfBox + row_off, &p.kmap[loc.tier], h * 64, loc.row, kvh, loc.slab, fb, pol);
+                tma_load_4d(vdst + h * kHalfBox + row_off, &p.vmap[loc.tier], h * 64, loc.row, kvh, loc.slab, fb, pol);
+              }
+            }
+            issued_mask |= 1u << s;
+            issued_par = (issued_par & ~(1u << s)) | (ph << s);
           }
         }
-        issued_mask |= 1u << s;
-        issued_par = (issued_par & ~(1u << s)) | (ph << s);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       }
-      if (*abort_flag) {
+      if (lane == 0 && *abort_flag) {
         const WaitCtx drain{reinterpret_cast<volatile int *>(smem + S::flag_off + 4), p.status};
         *drain.abort = 0;
         for (int st = 0; st < kAttnStages; ++st)
@@ -188,153 +240,173 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
   }
 
   // ---------------------------------------------------------------- compute
-  const int tid = threadIdx.x;          // 0..127
-  const int qt = tid >> 1;              // q.k: token of this thread
-  const int qh = tid & 1;               //      and which 64-dim half
-  const int vd = 4 * lane;              // p.V: 4 dims d0..d0+3 of this thread
-  const int vh = vd >> 6;               //      their 64-dim box
-  const int vc = (vd & 63) >> 3;        //      logical 16-byte chunk in the box row
-  const int vw = (vd & 7) * 2;          //      byte offset inside the chunk
-  float m_run[G], l_part[G], o[G][4];
+  // Tensor cores (mma.sync m16n8k16, FP32 accumulators).  Warp w owns tokens
+  // 16w .. 16w+15 of every chunk and keeps its own online softmax; the four
+  // warps' (m, l, o) are merged once at the end.  The G query heads of the
+  // group are the M rows (rows G..15 are zero):
+  //   S[16 x 16 tokens] = Q[16 x 128] . K^T      (8 k-steps x 2 token tiles)
+  //   O[16 x 128]      += P[16 x 16] . V[16 x 128] (16 dim tiles)
+  // P is rounded to the input type before P.V, as transformers' eager path
+  // does (softmax in FP32, then cast to the query dtype).
+  const int r = lane >> 2;   // fragment row: query head
+  const int cq = lane & 3;   // fragment column pair
+  const int tw = 16 * warp;  // this warp's first token in a chunk
+  uint32_t qa[8][4];
+  {
+    const uint32_t *qrow = nullptr;
+    if (r < G)
+      qrow = reinterpret_cast<const uint32_t *>(reinterpret_cast<const uint16_t *>(p.query) + (long long)b * p.q_stride_b +
+                                                (long long)(kvh * G + r) * p.q_stride_h);
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m_run[g] = -FLT_MAX;
-    l_part[g] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[g][j] = 0.f;
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = qrow ? qrow[(ks * 16 + cq * 2) / 2] : 0u;
+      qa[ks][1] = 0u;  // rows 8..15
+      qa[ks][2] = qrow ? qrow[(ks * 16 + cq * 2 + 8) / 2] : 0u;
+      qa[ks][3] = 0u;
+    }
   }
+  float m_run = -FLT_MAX, l_part = 0.f;  // row r of this warp
+  float o[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[nt][j] = 0.f;
 
   for (int c = 0; c < nchunks; ++c) {
     const int s = c % kAttnStages;
     const uint32_t ph = (uint32_t)((c / kAttnStages) & 1);
     const bool ok = mbar_wait<false>(full0 + 8 * s, ph, wc);
-    const uint8_t *kst = smem + S::kv_off + s * kStageBytes;
-    const uint8_t *vst = kst + kKvChunkBytes;
+    const uint32_t kst = sbase + S::kv_off + s * kStageBytes;
+    const uint32_t vst = kst + kKvChunkBytes;
     const int c0 = t_begin + c * kChunk;
     const int valid = ok ? min(kChunk, t_end - c0) : 0;
-
-    // ---- scores for token qt, dims qh*64 .. qh*64+63
-    float sc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) sc[g] = 0.f;
-    if (qt < valid) {
-      const uint8_t *krow = kst + qh * kHalfBox + qt * 128;
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        const uint4 kv = *reinterpret_cast<const uint4 *>(krow + ((cc ^ (qt & 7)) << 4));
-        const float2 k0 = Elem<T>::to_float2(kv.x), k1 = Elem<T>::to_float2(kv.y);
-        const float2 k2 = Elem<T>::to_float2(kv.z), k3 = Elem<T>::to_float2(kv.w);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float4 qa = *reinterpret_cast<const float4 *>(q_s + g * kHeadDim + qh * 64 + cc * 8);
-          const float4 qb = *reinterpret_cast<const float4 *>(q_s + g * kHeadDim + qh * 64 + cc * 8 + 4);
-          float a = sc[g];
-          a = fmaf(qa.x, k0.x, a); a = fmaf(qa.y, k0.y, a); a = fmaf(qa.z, k1.x, a); a = fmaf(qa.w, k1.y, a);
-          a = fmaf(qb.x, k2.x, a); a = fmaf(qb.y, k2.y, a); a = fmaf(qb.z, k3.x, a); a = fmaf(qb.w, k3.y, a);
-          sc[g] = a;
-        }
+    if (valid < kChunk) {
+      // Rows past the end hold stale bytes that P = 0 would still multiply:
+      // clear them (both 64-dim halves of V) before any warp reads V.
+      uint8_t *vgen = smem + S::kv_off + s * kStageBytes + kKvChunkBytes;
+      for (int i = threadIdx.x; i < (kChunk - valid) * 16; i += kAttnComputeWarps * 32) {
+        const int row = valid + i / 16, piece = i % 16;
+        *reinterpret_cast<uint4 *>(vgen + (piece >> 3) * kHalfBox + row * 128 + (piece & 7) * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
       }
+      named_sync(1, kAttnComputeWarps * 32);
     }
-    const float mval = (p.mask && qt < valid) ? p.mask[(long long)b * p.mask_stride_b + c0 + qt] : 0.f;
-    float wmax[G];
+
+    if (tw < valid) {
+      // ---- S = Q . K^T for tokens tw .. tw+15
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float v = sc[g] + __shfl_xor_sync(0xffffffffu, sc[g], 1);
-      v = qt < valid ? v * p.scaling + mval : -FLT_MAX;
-      sc[g] = v;
-      float mx = v;
+      for (int ks = 0; ks < 8; ++ks) {
+        // matrix j: tokens tw + 8*(j>>1) + (lane&7), 8 dims at 16-byte chunk (ks%4)*2 + (j&1)
+        const int j = lane >> 3;
+        const int row = tw + 8 * (j >> 1) + (lane & 7);
+        const int ch = (ks & 3) * 2 + (j & 1);
+        const uint32_t addr = kst + (ks >> 2) * kHalfBox + row * 128 + ((ch ^ (row & 7)) << 4);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(addr, b00, b01, b10, b11);
+        Mma<T>::run(sc[0], qa[ks], b00, b01);
+        Mma<T>::run(sc[1], qa[ks], b10, b11);
+      }
+      // ---- online softmax of row r over this warp's 16 tokens
+      float v[4];
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = tw + nt * 8 + cq * 2 + e;
+          float x = sc[nt][e] * p.scaling;
+          if (p.mask && t < valid) x += p.mask[(long long)b * p.mask_stride_b + c0 + t];
+          x = t < valid ? x : -FLT_MAX;
+          v[nt * 2 + e] = x;
+          mx = fmaxf(mx, x);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      wmax[g] = mx;
-    }
-    float *rm = redmax + (c & 1) * kAttnComputeWarps * kMaxGroup;
-    if (lane == 0)
+      const float mn = fmaxf(m_run, mx);
+      const float alpha = (m_run == -FLT_MAX) ? 0.f : expf(m_run - mn);
+      float pr[4];
 #pragma unroll
-      for (int g = 0; g < G; ++g) rm[warp * kMaxGroup + g] = wmax[g];
-    named_sync(1, kAttnComputeWarps * 32);
-
-    // ---- online softmax update
-    float alpha[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float mc = rm[g];
-#pragma unroll
-      for (int w = 1; w < kAttnComputeWarps; ++w) mc = fmaxf(mc, rm[w * kMaxGroup + g]);
-      const float mn = fmaxf(m_run[g], mc);
-      alpha[g] = (m_run[g] == -FLT_MAX) ? 0.f : expf(m_run[g] - mn);
-      const float pv = (qt < valid && mn != -FLT_MAX) ? expf(sc[g] - mn) : 0.f;
-      if (qh == 0) p_s[qt * kMaxGroup + g] = pv;
-      l_part[g] = l_part[g] * alpha[g] + (qh == 0 ? pv : 0.f);
-      m_run[g] = mn;
-    }
-    named_sync(1, kAttnComputeWarps * 32);
-
-    // ---- o += p . V over this warp's tokens (t = warp, warp+4, ...)
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[g][j] *= alpha[g];
-    for (int t = warp; t < valid; t += kAttnComputeWarps) {
-      const uint2 vv = *reinterpret_cast<const uint2 *>(vst + vh * kHalfBox + t * 128 + ((vc ^ (t & 7)) << 4) + vw);
-      const float2 v0 = Elem<T>::to_float2(vv.x), v1 = Elem<T>::to_float2(vv.y);
-      float pg[G];
-      if (G >= 4) {
-#pragma unroll
-        for (int g = 0; g < G; g += 4) {
-          const float4 pp = *reinterpret_cast<const float4 *>(p_s + t * kMaxGroup + g);
-          pg[g] = pp.x; pg[g + 1] = pp.y; pg[g + 2] = pp.z; pg[g + 3] = pp.w;
-        }
-      } else {
-#pragma unroll
-        for (int g = 0; g < G; ++g) pg[g] = p_s[t * kMaxGroup + g];
+      for (int e = 0; e < 4; ++e) pr[e] = (v[e] == -FLT_MAX || mn == -FLT_MAX) ? 0.f : expf(v[e] - mn);
+      m_run = mn;
+      // Round P to the input type; l sums the rounded values P.V will use.
+      uint32_t pa[4];
+      pa[0] = Elem<T>::pack2(pr[0], pr[1]);
+      pa[1] = 0u;
+      pa[2] = Elem<T>::pack2(pr[2], pr[3]);
+      pa[3] = 0u;
+      {
+        const float2 p01 = Elem<T>::to_float2(pa[0]), p23 = Elem<T>::to_float2(pa[2]);
+        l_part = l_part * alpha + (p01.x + p01.y + p23.x + p23.y);
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        o[g][0] = fmaf(pg[g], v0.x, o[g][0]);
-        o[g][1] = fmaf(pg[g], v0.y, o[g][1]);
-        o[g][2] = fmaf(pg[g], v1.x, o[g][2]);
-        o[g][3] = fmaf(pg[g], v1.y, o[g][3]);
+      for (int nt = 0; nt < 16; ++nt) {
+        o[nt][0] *= alpha;
+        o[nt][1] *= alpha;
       }
+      // ---- O += P . V over tokens tw .. tw+15, dims in 16 tiles of 8
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        // matrix j: tokens tw + 8*(j&1) + (lane&7), dims chunk 2*np + (j>>1) (transposed)
+        const int j = lane >> 3;
+        const int row = tw + 8 * (j & 1) + (lane & 7);
+        const int dch = 2 * np + (j >> 1);
+        const uint32_t addr = vst + (dch >> 3) * kHalfBox + row * 128 + (((dch & 7) ^ (row & 7)) << 4);
+        uint32_t b0a, b1a, b0b, b1b;
+        ldsm_x4_t(addr, b0a, b1a, b0b, b1b);
+        Mma<T>::run(o[2 * np], pa, b0a, b1a);
+        Mma<T>::run(o[2 * np + 1], pa, b0b, b1b);
+      }
+    }
+    if (valid < kChunk) {
+      // The stage's next fill comes from the async proxy.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
   }
 
-  // ---- combine the 4 warps' partial o and the 128 threads' partial l
+  // ---- merge the 4 warps: row r of warp w holds (m, l, o[dims])
+  float l = l_part;
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  float *mred = redmax;                                  // [warp][G]
+  float *lr = lred;                                      // [warp][G]
+  if (r < G) {
+    if (cq == 0) {
+      mred[warp * kMaxGroup + r] = m_run;
+      lr[warp * kMaxGroup + r] = l;
+    }
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float l = l_part[g];
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    l += __shfl_xor_sync(0xffffffffu, l, 4);
-    l += __shfl_xor_sync(0xffffffffu, l, 8);
-    l += __shfl_xor_sync(0xffffffffu, l, 16);
-    if (lane == 0) lred[warp * kMaxGroup + g] = l;
-    *reinterpret_cast<float4 *>(ored + (warp * kMaxGroup + g) * kHeadDim + vd) =
-        make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+    for (int nt = 0; nt < 16; ++nt)
+      *reinterpret_cast<float2 *>(ored + (warp * kMaxGroup + r) * kHeadDim + nt * 8 + cq * 2) =
+          make_float2(o[nt][0], o[nt][1]);
   }
   named_sync(1, kAttnComputeWarps * 32);
-  // Thread tid finishes dim (tid) of every head.
-  const int d = tid;
+  // Thread tid finishes dim tid of every head.
+  const int d = threadIdx.x;
   for (int g = 0; g < G; ++g) {
-    float acc = 0.f, l = 0.f;
+    float gm = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < kAttnComputeWarps; ++w) gm = fmaxf(gm, mred[w * kMaxGroup + g]);
+    float acc = 0.f, den = 0.f;
 #pragma unroll
     for (int w = 0; w < kAttnComputeWarps; ++w) {
-      acc += ored[(w * kMaxGroup + g) * kHeadDim + d];
-      l += lred[w * kMaxGroup + g];
+      const float mw = mred[w * kMaxGroup + g];
+      const float sc = (mw == -FLT_MAX) ? 0.f : expf(mw - gm);
+      acc += ored[(w * kMaxGroup + g) * kHeadDim + d] * sc;
+      den += lr[w * kMaxGroup + g] * sc;
     }
     const int hq = kvh * G + g;
     if (p.num_splits == 1) {
       uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + (long long)b * p.o_stride_b + (long long)hq * p.o_stride_h;
-      out[d] = Elem<T>::from_float(l == 0.f ? 0.f : acc / l);
+      out[d] = Elem<T>::from_float(den == 0.f ? 0.f : acc / den);
     } else {
       const long long base = ((long long)b * p.num_q_heads + hq) * p.num_splits + split;
       p.partial_o[base * kHeadDim + d] = acc;
       if (d == 0) {
-        p.partial_ml[base * 2] = m_run[g];
-        p.partial_ml[base * 2 + 1] = l;
+        p.partial_ml[base * 2] = gm;
+        p.partial_ml[base * 2 + 1] = den;
       }
     }
   }
