@@ -1,0 +1,42 @@
+"""Host-side planning helpers (no GPU): the per-rank host fractions that balance
+the host streams of a tensor-parallel decode, and the attention split size."""
+import math
+
+import pytest
+
+import bench
+from directaccesskernel_b200.attention import auto_split_size
+
+
+def test_balanced_host_fractions_keep_the_mean_and_follow_bandwidth():
+    bw = [35.0] * 4 + [23.0] * 4
+    f = bench.balanced_host_fractions(0.81, bw)
+    assert sum(f) / len(f) == pytest.approx(0.81)
+    # host bytes / bandwidth equal on every rank: the host streams finish together
+    t = [fi / b for fi, b in zip(f, bw)]
+    assert max(t) == pytest.approx(min(t))
+
+
+def test_balanced_host_fractions_clamp_and_redistribute():
+    f = bench.balanced_host_fractions(0.9, [35.0] * 4 + [23.0] * 4)
+    assert all(0.0 <= x <= 1.0 for x in f)
+    assert f[:4] == [1.0] * 4
+    assert sum(f) / len(f) == pytest.approx(0.9)
+    g = bench.balanced_host_fractions(0.5, [100.0, 1.0], lo=0.3)
+    assert g[1] == pytest.approx(0.3) and g[0] == pytest.approx(0.7)
+    assert bench.balanced_host_fractions(0.4, [50.0, 50.0]) == pytest.approx([0.4, 0.4])
+
+
+@pytest.mark.parametrize("batch,heads,seq", [(32, 1, 16394), (8, 8, 32768), (1, 8, 640), (3, 2, 75), (64, 8, 4096)])
+def test_auto_split_size_fills_whole_waves(batch, heads, seq):
+    sp = auto_split_size(batch, heads, seq, num_sms=148)
+    assert sp % 64 == 0 and sp >= 64
+    splits = math.ceil(seq / sp)
+    ctas = batch * heads * splits
+    # never worse than the old rule of about four waves
+    want = max(1, (4 * 148 + batch * heads - 1) // (batch * heads))
+    old = max(64, math.ceil(seq / want / 64) * 64)
+    old_splits = math.ceil(seq / old)
+    cost = lambda s, n: math.ceil(batch * heads * n / 148) * (s // 64 + 2)  # noqa: E731
+    assert cost(sp, splits) <= cost(old, old_splits)
+    assert ctas >= 1
