@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
     ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
     ap.add_argument("--ctx", type=int, default=16384, help="llama70b: context tokens per sequence")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="llama70b: NCCL all-reduce after o and down instead of the fused kernel")
     ap.add_argument("--no-balance", action="store_true",
                     help="llama70b: same host fraction on every rank (default: balanced by host bandwidth)")
     ap.add_argument("--host-fraction", type=float, default=None,
@@ -701,7 +703,9 @@ def run_llama70b(args, torch, rank, world):
         raise SystemExit(f"llama70b at TP{world}: {host_need / 1e9:.0f} GB of pinned host memory needed, more than "
                          f"3/4 of the box's {ram / 1e9:.0f} GB; use --layers / --host-fraction")
     t0 = time.perf_counter()
-    dec = TPLlamaDecoder(shape, batch=B, max_ctx=max_ctx, weight_offload=my_frac, kv_host_fraction=my_frac)
+    fused = world > 1 and not args.nccl_allreduce
+    dec = TPLlamaDecoder(shape, batch=B, max_ctx=max_ctx, weight_offload=my_frac, kv_host_fraction=my_frac,
+                         fused_allreduce=fused)
     dec.init_random(seed=0)
     dec.fill_kv_random(ctx, seed=1)
     g = torch.Generator().manual_seed(3)
@@ -783,7 +787,9 @@ def run_llama70b(args, torch, rank, world):
                    "host_fraction": round(frac, 4), "per_rank_host_fractions": [round(f, 4) for f in fracs],
                    "rank0_host_bytes": int(lin_host + kv_host),
                    "rank0_device_bytes": int(lin_dev + kv_dev), "build_s": round(build_s, 1),
-                   "parallelism": f"tp{world}", "l2": "tens of GB read per step exceed L2",
+                   "parallelism": f"tp{world}", "allreduce": "fused into the o/down kernels over NVLink peer "
+                                                               "memory" if fused else "NCCL",
+                   "l2": "tens of GB read per step exceed L2",
                    "timing": "CUDA events around K graph replays, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": round((host_step + dev_step) / (step_ms * 1e-3) / 1e9, 2),
                      "peak": round((host_step + dev_step) / (roof_ms * 1e-3) / 1e9, 2), "unit": "GB/s",

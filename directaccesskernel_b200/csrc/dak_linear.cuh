@@ -66,6 +66,27 @@ struct GroupWork {
   }
 };
 
+// Row-parallel all-reduce fused into the tcgen05 linear kernel (one-shot, over
+// peer memory).  Every rank holds, in memory mapped into all ranks, a receive
+// buffer of 2 parities x world slots of [ntok, ldy] 16-bit partials and a flag
+// array of [max_ctas][world] epochs.  Call e (e = *epoch + 1) writes its
+// partial outputs into slot `rank` of parity e & 1 on every rank, sets flag
+// [cta][rank] = e on every rank (system-scope release), waits until every
+// rank's flag [cta][*] reached e (bounded), and sums the slots into y.  The
+// last CTA to finish bumps *epoch.  All ranks run the same shapes, hence the
+// same plan, and the grid is one resident wave, so peer CTAs run together.
+constexpr int kArMaxRanks = 8;
+constexpr int kArMaxCtas = 1024;
+struct ArParams {
+  uint16_t *buf[kArMaxRanks];    // each rank's receive buffer (this process's mapping)
+  uint32_t *flags[kArMaxRanks];  // each rank's flag array
+  long long slot_elems;          // 16-bit elements per slot
+  int *epoch;                    // this rank's call counter (device memory)
+  int *done;                     // this rank's finished-CTA counter
+  int world, rank;
+  long long timeout_ns;
+};
+
 struct alignas(64) LinearParams {
   LinearTier tier[2];  // [0] host tier, [1] device tier
   CUtensorMap xmap;    // x[ntok, K] activations
@@ -78,7 +99,8 @@ struct alignas(64) LinearParams {
   int stages;          // pipeline depth (tcgen05 kernel; sized to the shared memory left)
   int pdl;             // launched with programmatic stream serialization: weights are
                        // prefetched before griddepcontrol.wait, x and y only after it
-  int pad_[1];
+  int ar_on;           // 1: y is the all-reduce (sum over ranks) of this kernel's result
+  ArParams ar;
 };
 
 }  // namespace dak

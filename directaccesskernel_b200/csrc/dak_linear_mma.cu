@@ -159,6 +159,17 @@ __host__ __device__ constexpr uint32_t mma_idesc(int ntokp) {
          | ((uint32_t)(kMmaBM >> 4) << 24);                    // M >> 4
 }
 
+// System-scope release store / acquire load of a 32-bit flag in (possibly peer)
+// global memory, for the fused all-reduce.
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 template <typename T, int NTOKP>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     linear_mma_kernel(const __grid_constant__ LinearParams p) {
@@ -337,6 +348,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
     int n = 0;
     int nred = 0;
+    // Fused all-reduce: this call's epoch, and where this rank's partial goes in
+    // every rank's receive buffer (slot `rank` of parity epoch & 1).
+    const uint32_t ar_epoch = p.ar_on ? (uint32_t)(*reinterpret_cast<volatile int *>(p.ar.epoch) + 1) : 0u;
+    const long long ar_slot =
+        p.ar_on ? ((long long)(ar_epoch & 1u) * p.ar.world + p.ar.rank) * p.ar.slot_elems : 0;
     if (kb1 > kb0) {
       for (int j = 0; j < ntiles; ++j, ++n) {
         const int ab = n & 1;
@@ -366,11 +382,22 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               }
             }
             if (col_ok) {
+              if (p.ar_on) {
+                const long long base = ar_slot + tier.col_offset + col;
 #pragma unroll
-              for (int j = 0; j < kChunkCols; ++j)
-                if (c0 + j < p.ntok)
-                  reinterpret_cast<uint16_t *>(ycol)[(long long)(c0 + j) * p.ldy] =
-                      Elem<T>::from_float(v[j]);
+                for (int j = 0; j < kChunkCols; ++j)
+                  if (c0 + j < p.ntok) {
+                    const uint16_t h = Elem<T>::from_float(v[j]);
+                    for (int rk = 0; rk < p.ar.world; ++rk)
+                      p.ar.buf[rk][base + (long long)(c0 + j) * p.ldy] = h;
+                  }
+              } else {
+#pragma unroll
+                for (int j = 0; j < kChunkCols; ++j)
+                  if (c0 + j < p.ntok)
+                    reinterpret_cast<uint16_t *>(ycol)[(long long)(c0 + j) * p.ldy] =
+                        Elem<T>::from_float(v[j]);
+              }
             }
           }
           if (ks > 1) {
@@ -402,6 +429,53 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(tempty0 + 8 * ab);
       }
+    }
+    if (p.ar_on) {
+      // ---- fused all-reduce: publish, wait for every rank's same CTA, sum
+      const int W = p.ar.world, me = p.ar.rank, c = (int)blockIdx.x;
+      volatile int *ar_fail = abort_flag + 2;
+      __threadfence_system();
+      named_sync(2, kMmaEpiWarps * 32);
+      if (warp == 2 && lane == 0) {
+        *ar_fail = 0;
+        for (int rk = 0; rk < W; ++rk) st_release_sys(p.ar.flags[rk] + (long long)c * W + me, ar_epoch);
+        const unsigned long long t0 = globaltimer();
+        for (int rk = 0; rk < W && !*ar_fail; ++rk)
+          while ((int)(ld_acquire_sys(p.ar.flags[me] + (long long)c * W + rk) - ar_epoch) < 0) {
+            if (globaltimer() - t0 > (unsigned long long)p.ar.timeout_ns) {
+              atomicCAS(p.status, 0, DAK_ERR_TIMEOUT);
+              *ar_fail = 1;
+              break;
+            }
+          }
+      }
+      __syncwarp();
+      named_sync(2, kMmaEpiWarps * 32);
+      if (!*ar_fail && kb1 > kb0) {
+        const uint16_t *rb = p.ar.buf[me] + (long long)(ar_epoch & 1u) * W * p.ar.slot_elems;
+        for (int j = 0; j < ntiles; ++j) {
+          const int col = tile_box0(j) * kBoxCols + f;
+          const bool col_ok = f < tile_nbox(j) * kBoxCols && col < tier.cols;
+          if (!col_ok || !(ks == 1 || owner == r)) continue;
+          const long long cidx = tier.col_offset + col;
+          for (int row = 0; row < p.ntok; ++row) {
+            const long long idx = (long long)row * p.ldy + cidx;
+            float acc = 0.f;
+            for (int rk = 0; rk < W; ++rk) acc += Elem<T>::to_float(rb[(long long)rk * p.ar.slot_elems + idx]);
+            reinterpret_cast<uint16_t *>(p.y)[idx] = Elem<T>::from_float(acc);
+          }
+        }
+      }
+      named_sync(2, kMmaEpiWarps * 32);
+      if (warp == 2 && lane == 0) {
+        __threadfence();
+        if (atomicAdd(p.ar.done, 1) == (int)gridDim.x - 1) {
+          *p.ar.done = 0;
+          __threadfence();
+          atomicExch(p.ar.epoch, (int)ar_epoch);
+        }
+      }
+      __syncwarp();
     }
   }
 

@@ -398,7 +398,7 @@ int check_ptr16(const void *p, const char *what) {
   return DAK_OK;
 }
 
-int run_linear(const dak_linear_args *a, cudaStream_t stream) {
+int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar = nullptr) {
   if (!a) return fail(DAK_ERR_INVALID_ARG, "args is null");
   if (a->dtype != DAK_DTYPE_F16 && a->dtype != DAK_DTYPE_BF16)
     return fail(DAK_ERR_UNSUPPORTED, "linear supports float16 and bfloat16 only");
@@ -433,6 +433,12 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream) {
 
   int path = a->path;
   if (path == DAK_PATH_AUTO) path = a->ntok <= kCoreAutoMaxTok ? DAK_PATH_CUDA_CORE : DAK_PATH_TCGEN05;
+  if (ar) {
+    // The fused all-reduce lives in the tcgen05 kernel, which serves any token count.
+    if (a->path == DAK_PATH_CUDA_CORE)
+      return fail(DAK_ERR_UNSUPPORTED, "the fused all-reduce runs on the tcgen05 path");
+    path = DAK_PATH_TCGEN05;
+  }
   if (path == DAK_PATH_CUDA_CORE && a->ntok > kCoreMaxTok)
     return fail(DAK_ERR_INVALID_ARG, "CUDA-core path serves at most %d tokens", kCoreMaxTok);
   const bool mma = path == DAK_PATH_TCGEN05;
@@ -572,6 +578,14 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream) {
     p.status = dev->status;
     p.red_slots = cluster - 1;
     p.pdl = pdl_enabled() ? 1 : 0;
+    if (ar) {
+      if (grid > kArMaxCtas) return fail(DAK_ERR_UNSUPPORTED, "fused all-reduce: grid of %d CTAs", grid);
+      if (ar->slot_elems < nt * a->ldy)
+        return fail(DAK_ERR_INVALID_ARG, "fused all-reduce: slot_elems %lld below %lld x ldy",
+                    (long long)ar->slot_elems, (long long)nt);
+      p.ar_on = 1;
+      p.ar = *ar;
+    }
 
     size_t smem;
     cudaError_t e;
@@ -853,6 +867,30 @@ int dak_tensormap_replace_address(void *desc, const void *new_base) {
 
 int dak_linear_split(const dak_linear_args *args, void *stream) {
   return run_linear(args, static_cast<cudaStream_t>(stream));
+}
+
+int dak_linear_split_allreduce(const dak_linear_args *args, const dak_allreduce_args *ar, void *stream) {
+  if (!ar) return fail(DAK_ERR_INVALID_ARG, "all-reduce args are null");
+  if (ar->world < 1 || ar->world > kArMaxRanks || ar->rank < 0 || ar->rank >= ar->world)
+    return fail(DAK_ERR_INVALID_ARG, "world must be 1..%d and rank in [0, world)", kArMaxRanks);
+  if (!ar->epoch || !ar->done || ar->slot_elems <= 0 || ar->timeout_us <= 0)
+    return fail(DAK_ERR_INVALID_ARG, "epoch, done, slot_elems and timeout_us are required");
+  ArParams p;
+  std::memset(&p, 0, sizeof(p));
+  for (int r = 0; r < ar->world; ++r) {
+    if (!ar->buffers[r] || !ar->flags[r]) return fail(DAK_ERR_INVALID_ARG, "rank %d buffer or flags missing", r);
+    if ((reinterpret_cast<uintptr_t>(ar->buffers[r]) & 15u) || (reinterpret_cast<uintptr_t>(ar->flags[r]) & 3u))
+      return fail(DAK_ERR_ALIGNMENT, "rank %d buffer must be 16-byte aligned, flags 4-byte aligned", r);
+    p.buf[r] = static_cast<uint16_t *>(ar->buffers[r]);
+    p.flags[r] = ar->flags[r];
+  }
+  p.slot_elems = ar->slot_elems;
+  p.epoch = ar->epoch;
+  p.done = ar->done;
+  p.world = ar->world;
+  p.rank = ar->rank;
+  p.timeout_ns = ar->timeout_us * 1000;
+  return run_linear(args, static_cast<cudaStream_t>(stream), &p);
 }
 
 int dak_gemv(const void *a_desc, const void *b_desc, const void *c_desc, int M, int N, int K,

@@ -98,7 +98,8 @@ class TPLlamaDecoder(nn.Module):
     pages).  ``max_ctx`` bounds the tokens a sequence can hold."""
 
     def __init__(self, shape: LlamaShape, *, batch: int, max_ctx: int, weight_offload: float = 0.0,
-                 kv_host_fraction: float = 0.0, group=None, dtype=torch.float16, device="cuda"):
+                 kv_host_fraction: float = 0.0, group=None, dtype=torch.float16, device="cuda",
+                 fused_allreduce: bool = False):
         super().__init__()
         self.s = shape
         self.group = group
@@ -123,6 +124,13 @@ class TPLlamaDecoder(nn.Module):
         self._alloc_kv()
         self._alloc_buffers()
         self.graph = None
+        # o and down with their all-reduce fused into the linear kernel (peer
+        # memory over NVLink) instead of a separate NCCL all-reduce.
+        self.ar = None
+        if fused_allreduce:
+            from .tp import SymmetricAllReduce
+
+            self.ar = SymmetricAllReduce(batch * shape.hidden, group=group, dtype=dtype)
 
     # ------------------------------------------------------------- weights
     def _make_linear(self, w: torch.Tensor) -> nn.Module:
@@ -263,6 +271,8 @@ class TPLlamaDecoder(nn.Module):
         self.k_buf = torch.empty(B, self.hkv, d, dtype=self.dtype, device=self.device)
         self.v_buf = torch.empty(B, self.hkv, d, dtype=self.dtype, device=self.device)
         self.act_buf = torch.empty(B, self.ffn_r, dtype=self.dtype, device=self.device)
+        self.o_buf = torch.empty(B, h, dtype=self.dtype, device=self.device)
+        self.dn_buf = torch.empty(B, h, dtype=self.dtype, device=self.device)
 
     def set_positions(self, pos: int) -> None:
         self.pos.fill_(pos)
@@ -270,6 +280,22 @@ class TPLlamaDecoder(nn.Module):
     def _all_reduce(self, t: torch.Tensor) -> None:
         if self.world > 1:
             dist.all_reduce(t, group=self.group)
+
+    def _row_parallel(self, mod: nn.Module, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """A row-parallel projection summed over the ranks: the fused kernel when
+        enabled, else the local linear followed by an NCCL all-reduce."""
+        if self.ar is None:
+            y = mod(x)
+            self._all_reduce(y)
+            return y
+        from .runtime import linear_split
+
+        if hasattr(mod, "weight_h"):
+            wh = mod.weight_h if mod.out_features_h > 0 else None
+            wd = mod.weight_d if mod.out_features_d > 0 else None
+        else:
+            wh, wd = (None, mod.weight) if mod.weight.is_cuda else (mod.weight, None)
+        return linear_split(x, out, wh, wd, allreduce=self.ar)
 
     def forward_step(self, keep_logits: bool = False) -> torch.Tensor:
         """One decode step on the static buffers: embeds ``ids`` at ``pos``, writes
@@ -292,12 +318,10 @@ class TPLlamaDecoder(nn.Module):
             decode_paged(self.q_buf, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale, self.split,
                          out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
                          max_seq_len=self.max_ctx)
-            o = layer.o(self.attn_out.view(B, qd))
-            self._all_reduce(o)
+            o = self._row_parallel(layer.o, self.attn_out.view(B, qd), self.o_buf)
             x = rmsnorm(o, layer.post_w, s.eps, residual=self.hidden, out=self.x_buf)
             gu = layer.gate_up(x)
-            dn = layer.down(silu_mul(gu, out=self.act_buf))
-            self._all_reduce(dn)
+            dn = self._row_parallel(layer.down, silu_mul(gu, out=self.act_buf), self.dn_buf)
             nxt_w = self.layers[l + 1].in_w if l + 1 < len(self.layers) else self.final_w
             x = rmsnorm(dn, nxt_w, s.eps, residual=self.hidden, out=self.x_buf)
         logits = self.lm_head(x)[:, :max(1, self.vocab_valid)]

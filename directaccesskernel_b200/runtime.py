@@ -178,11 +178,14 @@ def _i64(v) -> int:
 
 def linear_split(x: torch.Tensor, y: torch.Tensor, w_host: torch.Tensor | None, w_dev: torch.Tensor | None,
                  host_col_offset: int = 0, dev_col_offset: int | None = None, *, host_ctas: int = 0,
-                 dev_ctas: int = 0, host_ksplit: int = 0, dev_ksplit: int = 0, path: int = _lib.PATH_AUTO) -> torch.Tensor:
+                 dev_ctas: int = 0, host_ksplit: int = 0, dev_ksplit: int = 0, path: int = _lib.PATH_AUTO,
+                 allreduce=None) -> torch.Tensor:
     """y[:, off:off+cols] = x @ w for each tier, with w the transposed weight [K, cols].
 
     ``x`` is [ntok, K] (row-major, last dim contiguous), ``y`` [ntok, ldy];
     ``w_host`` lives in pinned host memory, ``w_dev`` in HBM; either may be None.
+    With ``allreduce`` (a ``tp.SymmetricAllReduce``), y is summed over the ranks
+    of its group inside the same kernel (row-parallel layers).
     """
     if x.dim() != 2 or y.dim() != 2 or x.stride(1) != 1 or y.stride(1) != 1:
         raise RuntimeError("x and y must be 2-D with a contiguous last dimension")
@@ -208,7 +211,11 @@ def linear_split(x: torch.Tensor, y: torch.Tensor, w_host: torch.Tensor | None, 
     a.y, a.ldy = y.data_ptr(), y.stride(0)
     a.ntok, a.K, a.dtype = ntok, K, dak_dtype(x.dtype)
     a.host_ctas, a.dev_ctas, a.host_ksplit, a.dev_ksplit, a.path = host_ctas, dev_ctas, host_ksplit, dev_ksplit, path
-    check(LIB.dak_linear_split(ctypes.byref(a), _stream_ptr()), "linear_split")
+    if allreduce is not None:
+        check(LIB.dak_linear_split_allreduce(ctypes.byref(a), ctypes.byref(allreduce.args(y)), _stream_ptr()),
+              "linear_split_allreduce")
+    else:
+        check(LIB.dak_linear_split(ctypes.byref(a), _stream_ptr()), "linear_split")
     return y
 
 

@@ -108,3 +108,51 @@ def make_offloaded_shard(weight_shard: torch.Tensor, offload_ratio: float, *, ho
         mod.move_weight_to_device("cpu" if offload_ratio >= 1.0 else "cuda")
     mod.build_tma_desc()
     return mod
+
+
+class SymmetricAllReduce:
+    """Buffers for the all-reduce fused into the linear kernel
+    (``dak_linear_split_allreduce``): a receive buffer of 2 x world slots of
+    ``slot_elems`` 16-bit values and a flag array per rank, in torch symmetric
+    memory (mapped into every rank of ``group``), plus this rank's call
+    counters.  One instance serves any number of sequential calls on one
+    stream; every rank must make the same calls in the same order."""
+
+    MAX_CTAS = 1024
+
+    def __init__(self, slot_elems: int, group=None, dtype=torch.float16, timeout_us: int = 2_000_000):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank, self.world = _group_info(self.group)
+        if self.world > 8:
+            raise ValueError("the fused all-reduce serves at most 8 ranks")
+        self.slot_elems = int(slot_elems)
+        self.buf = symm_mem.empty(2 * self.world * self.slot_elems, dtype=dtype, device="cuda")
+        self.flags = symm_mem.empty(self.MAX_CTAS * self.world, dtype=torch.int32, device="cuda")
+        self.flags.zero_()
+        torch.cuda.synchronize()
+        self._hb = symm_mem.rendezvous(self.buf, self.group.group_name)
+        self._hf = symm_mem.rendezvous(self.flags, self.group.group_name)
+        self.counters = torch.zeros(2, dtype=torch.int32, device="cuda")  # epoch, done
+        dist.barrier(group=self.group)
+        self.timeout_us = int(timeout_us)
+        self._args = None
+
+    def args(self, y: torch.Tensor):
+        from . import _lib
+
+        if y.shape[0] * y.stride(0) > self.slot_elems:
+            raise RuntimeError(f"output of {y.shape[0]} x {y.stride(0)} exceeds the slots of {self.slot_elems}")
+        if self._args is None:
+            a = _lib.AllReduceArgs()
+            a.world, a.rank = self.world, self.rank
+            for r in range(self.world):
+                a.buffers[r] = self._hb.buffer_ptrs[r]
+                a.flags[r] = self._hf.buffer_ptrs[r]
+            a.slot_elems = self.slot_elems
+            a.epoch = self.counters.data_ptr()
+            a.done = self.counters.data_ptr() + 4
+            a.timeout_us = self.timeout_us
+            self._args = a
+        return self._args

@@ -187,6 +187,30 @@ typedef struct dak_linear_args {
 } dak_linear_args;
 DAK_API int dak_linear_split(const dak_linear_args *args, void *stream);
 
+/* Row-parallel linear with its all-reduce fused into the same kernel (no
+ * reference counterpart; the reference has no multi-GPU path).  Every rank of a
+ * tensor-parallel group calls it with the same shapes; y receives the sum over
+ * ranks of x_rank . W_rank^T.  The tcgen05 kernel pushes each output tile's
+ * 16-bit partial into every rank's receive buffer over peer memory (plain
+ * stores), sets a per-CTA epoch flag on every rank, waits (bounded by
+ * timeout_us; DAK_ERR_TIMEOUT in the device error word) for the same CTA of
+ * every rank and sums the slots.  Buffers come from memory mapped into all
+ * ranks (e.g. torch symmetric memory):
+ *   buffers[r]: rank r's receive buffer, 2 x world x slot_elems 16-bit;
+ *   flags[r]:   rank r's flags, 1024 x world uint32, zero before the first call;
+ *   epoch/done: this rank's counters in device memory, zero before the first call.
+ * slot_elems >= min(ntok, 256) x ldy.  Stream-ordered, graph-capturable, no
+ * allocation; calls on one group must not overlap. */
+typedef struct dak_allreduce_args {
+  int world, rank;
+  void *buffers[8];
+  uint32_t *flags[8];
+  int64_t slot_elems;
+  int *epoch, *done;
+  int64_t timeout_us;
+} dak_allreduce_args;
+DAK_API int dak_linear_split_allreduce(const dak_linear_args *args, const dak_allreduce_args *ar, void *stream);
+
 /* flush_l2_cache (src/torch_runtime.cu:363-371; include/task/utils.cuh:3-14):
  * reads n floats of `dummy` past L2 and folds them into *sink. */
 DAK_API int dak_flush_l2_cache(float *dummy, size_t n, float *sink, void *stream);

@@ -1,0 +1,101 @@
+"""Row-parallel linear with its all-reduce fused into the tcgen05 kernel
+(dak_linear_split_allreduce) against the unfused path: per-rank linear plus an
+NCCL all-reduce.  Runs with as many ranks as the box has GPUs (1 or 2 here),
+over several consecutive calls (epochs and buffer parities) and CUDA-graph
+replays, with weights split between pinned host memory and HBM."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).abs().max() / b.float().abs().max())
+
+
+def _worker(rank, world, port, q):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from directaccesskernel_b200 import runtime
+        from directaccesskernel_b200.tp import SymmetricAllReduce
+
+        errs = []
+        N, Kr = 4096, 1024
+        ar = SymmetricAllReduce(slot_elems=64 * N)
+        g = torch.Generator(device="cuda").manual_seed(100 + rank)
+        w = (torch.randn(Kr, N, generator=g, device="cuda") * 0.02).half()  # this rank's [K_r, N] shard
+        w_host = w[:, :1024].contiguous().cpu().pin_memory()
+        w_dev = w[:, 1024:].contiguous()
+        for ntok in (1, 32, 64, 32, 5):
+            x = torch.randn(ntok, Kr, generator=g, device="cuda").half()
+            y = torch.empty(ntok, N, dtype=torch.float16, device="cuda")
+            runtime.linear_split(x, y, w_host, w_dev, allreduce=ar)
+            ref = (x.float() @ w.float()).contiguous()
+            dist.all_reduce(ref)
+            errs.append(_rel(y, ref))
+        # CUDA graph: three fused calls captured, replayed twice with new inputs.
+        xs = [torch.randn(32, Kr, generator=g, device="cuda").half() for _ in range(3)]
+        ys = [torch.empty(32, N, dtype=torch.float16, device="cuda") for _ in range(3)]
+        for i in range(3):
+            runtime.linear_split(xs[i], ys[i], w_host, w_dev, allreduce=ar)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(3):
+                runtime.linear_split(xs[i], ys[i], w_host, w_dev, allreduce=ar)
+        for _ in range(2):
+            for i in range(3):
+                xs[i].copy_(torch.randn(32, Kr, generator=g, device="cuda").half())
+            graph.replay()
+            torch.cuda.synchronize()
+            for i in range(3):
+                ref = (xs[i].float() @ w.float()).contiguous()
+                dist.all_reduce(ref)
+                errs.append(_rel(ys[i], ref))
+        del graph
+        q.put((rank, max(errs), runtime.device_status()))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e), -1))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_fused_allreduce_matches_nccl(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, err, st = q.get(timeout=600)
+        res[r] = (err, st)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
+        err, st = res[r]
+        assert isinstance(err, float) and err <= 1e-2 and st == 0, res

@@ -101,7 +101,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _tp2_worker(rank, port, q):
+def _tp2_worker(rank, port, q, fused):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -118,7 +118,7 @@ def _tp2_worker(rank, port, q):
         g = torch.Generator().manual_seed(2)
         prompt = torch.randint(0, cfg.vocab_size, (2, 24), generator=g).cuda()
         dec = TPLlamaDecoder(LlamaShape.from_config(cfg), batch=2, max_ctx=32, weight_offload=0.5,
-                             kv_host_fraction=0.5).load_hf(hf)
+                             kv_host_fraction=0.5, fused_allreduce=fused).load_hf(hf)
         got = _teacher_forced(dec, prompt)
         with torch.inference_mode():
             ref = hf(input_ids=prompt).logits.float()
@@ -131,13 +131,14 @@ def _tp2_worker(rank, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_transformers():
+@pytest.mark.parametrize("fused", [False, True])
+def test_tp2_matches_transformers(fused):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp2_worker, args=(r, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_tp2_worker, args=(r, port, q, fused)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in procs)
