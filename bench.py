@@ -58,8 +58,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
     ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
     ap.add_argument("--ctx", type=int, default=16384, help="llama70b: context tokens per sequence")
-    ap.add_argument("--nccl-allreduce", action="store_true",
-                    help="llama70b: NCCL all-reduce after o and down instead of the fused kernel")
+    ap.add_argument("--fused-allreduce", action="store_true",
+                    help="llama70b: all-reduce of o and down fused into their kernels (default: NCCL)")
     ap.add_argument("--no-balance", action="store_true",
                     help="llama70b: same host fraction on every rank (default: balanced by host bandwidth)")
     ap.add_argument("--host-fraction", type=float, default=None,
@@ -703,7 +703,7 @@ def run_llama70b(args, torch, rank, world):
         raise SystemExit(f"llama70b at TP{world}: {host_need / 1e9:.0f} GB of pinned host memory needed, more than "
                          f"3/4 of the box's {ram / 1e9:.0f} GB; use --layers / --host-fraction")
     t0 = time.perf_counter()
-    fused = world > 1 and not args.nccl_allreduce
+    fused = world > 1 and args.fused_allreduce
     dec = TPLlamaDecoder(shape, batch=B, max_ctx=max_ctx, weight_offload=my_frac, kv_host_fraction=my_frac,
                          fused_allreduce=fused)
     dec.init_random(seed=0)
