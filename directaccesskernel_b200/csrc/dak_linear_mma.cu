@@ -170,7 +170,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   return v;
 }
 
-template <typename T, int NTOKP>
+template <typename T, int NTOKP, bool AR>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     linear_mma_kernel(const __grid_constant__ LinearParams p) {
   const MmaLayout<NTOKP> L(p.stages);
@@ -350,9 +350,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     int nred = 0;
     // Fused all-reduce: this call's epoch, and where this rank's partial goes in
     // every rank's receive buffer (slot `rank` of parity epoch & 1).
-    const uint32_t ar_epoch = p.ar_on ? (uint32_t)(*reinterpret_cast<volatile int *>(p.ar.epoch) + 1) : 0u;
+    const uint32_t ar_epoch = AR ? (uint32_t)(*reinterpret_cast<volatile int *>(p.ar.epoch) + 1) : 0u;
     const long long ar_slot =
-        p.ar_on ? ((long long)(ar_epoch & 1u) * p.ar.world + p.ar.rank) * p.ar.slot_elems : 0;
+        AR ? ((long long)(ar_epoch & 1u) * p.ar.world + p.ar.rank) * p.ar.slot_elems : 0;
     if (kb1 > kb0) {
       for (int j = 0; j < ntiles; ++j, ++n) {
         const int ab = n & 1;
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               }
             }
             if (col_ok) {
-              if (p.ar_on) {
+              if (AR) {
                 const long long base = ar_slot + tier.col_offset + col;
 #pragma unroll
                 for (int j = 0; j < kChunkCols; ++j)
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         if (lane == 0) mbar_arrive(tempty0 + 8 * ab);
       }
     }
-    if (p.ar_on) {
+    if (AR) {
       // ---- fused all-reduce: publish, wait for every rank's same CTA, sum
       const int W = p.ar.world, me = p.ar.rank, c = (int)blockIdx.x;
       volatile int *ar_fail = abort_flag + 2;
@@ -488,14 +488,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 template <typename T>
 cudaError_t launch_dtype(const LinearParams &p, int ntokp, int grid, int cluster, size_t smem,
                          cudaStream_t stream, int *mc) {
+  // The fused all-reduce is a separate instantiation, so the plain kernel
+  // carries none of its code or registers.
+#define DAK_MMA_CASE(N)                                                                                  \
+  case N:                                                                                                \
+    return p.ar_on ? launch_linear_kernel(linear_mma_kernel<T, N, true>, p, grid, kMmaThreads, cluster, smem, \
+                                          stream, mc)                                                    \
+                   : launch_linear_kernel(linear_mma_kernel<T, N, false>, p, grid, kMmaThreads, cluster, smem, \
+                                          stream, mc);
   switch (ntokp) {
-    case 16: return launch_linear_kernel(linear_mma_kernel<T, 16>, p, grid, kMmaThreads, cluster, smem, stream, mc);
-    case 32: return launch_linear_kernel(linear_mma_kernel<T, 32>, p, grid, kMmaThreads, cluster, smem, stream, mc);
-    case 64: return launch_linear_kernel(linear_mma_kernel<T, 64>, p, grid, kMmaThreads, cluster, smem, stream, mc);
-    case 128: return launch_linear_kernel(linear_mma_kernel<T, 128>, p, grid, kMmaThreads, cluster, smem, stream, mc);
-    case 256: return launch_linear_kernel(linear_mma_kernel<T, 256>, p, grid, kMmaThreads, cluster, smem, stream, mc);
+    DAK_MMA_CASE(16)
+    DAK_MMA_CASE(32)
+    DAK_MMA_CASE(64)
+    DAK_MMA_CASE(128)
+    DAK_MMA_CASE(256)
     default: return cudaErrorInvalidValue;
   }
+#undef DAK_MMA_CASE
 }
 
 template <int NTOKP>
