@@ -92,6 +92,7 @@ class AllReduceArgs(ctypes.Structure):
     _fields_ = [
         ("world", c_int), ("rank", c_int), ("buffers", c_vp * 8), ("flags", c_vp * 8),
         ("slot_elems", c_i64), ("epoch", c_vp), ("done", c_vp), ("timeout_us", c_i64),
+        ("own_f32", c_vp), ("mc_f32", c_vp),
     ]
 
 

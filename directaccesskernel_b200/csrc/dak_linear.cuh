@@ -77,9 +77,15 @@ struct GroupWork {
 // same plan, and the grid is one resident wave, so peer CTAs run together.
 constexpr int kArMaxRanks = 8;
 constexpr int kArMaxCtas = 1024;
+// With a multicast mapping (NVSwitch), the partials instead stay local: call e
+// stores its FP32 partials in this rank's own buffer (parity e & 1), publishes
+// the flags, and reads the sum over ranks with multimem.ld_reduce through the
+// multicast address, so each rank moves its data across NVLink once.
 struct ArParams {
   uint16_t *buf[kArMaxRanks];    // each rank's receive buffer (this process's mapping)
   uint32_t *flags[kArMaxRanks];  // each rank's flag array
+  float *own;                    // multicast mode: this rank's 2 x slot_elems FP32 buffer
+  float *mc;                     // multicast mode: the same buffer's multicast address
   long long slot_elems;          // 16-bit elements per slot
   int *epoch;                    // this rank's call counter (device memory)
   int *done;                     // this rank's finished-CTA counter

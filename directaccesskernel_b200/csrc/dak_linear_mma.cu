@@ -164,6 +164,14 @@ __host__ __device__ constexpr uint32_t mma_idesc(int ntokp) {
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Sum over all ranks of a 32-bit float at a multicast address (reduced in the switch).
+__device__ __forceinline__ float multimem_ld_reduce_add(const float *p) {
+  float v;
+  // No memory clobber: a batch of these is issued before any result is used;
+  // volatile keeps them after the barrier that follows the flag wait.
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -352,7 +360,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     // every rank's receive buffer (slot `rank` of parity epoch & 1).
     const uint32_t ar_epoch = AR ? (uint32_t)(*reinterpret_cast<volatile int *>(p.ar.epoch) + 1) : 0u;
     const long long ar_slot =
-        AR ? ((long long)(ar_epoch & 1u) * p.ar.world + p.ar.rank) * p.ar.slot_elems : 0;
+        !AR ? 0 : p.ar.mc ? (long long)(ar_epoch & 1u) * p.ar.slot_elems
+                          : ((long long)(ar_epoch & 1u) * p.ar.world + p.ar.rank) * p.ar.slot_elems;
     if (kb1 > kb0) {
       for (int j = 0; j < ntiles; ++j, ++n) {
         const int ab = n & 1;
@@ -384,13 +393,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             if (col_ok) {
               if (AR) {
                 const long long base = ar_slot + tier.col_offset + col;
+                if (p.ar.mc) {
 #pragma unroll
-                for (int j = 0; j < kChunkCols; ++j)
-                  if (c0 + j < p.ntok) {
-                    const uint16_t h = Elem<T>::from_float(v[j]);
-                    for (int rk = 0; rk < p.ar.world; ++rk)
-                      p.ar.buf[rk][base + (long long)(c0 + j) * p.ldy] = h;
-                  }
+                  for (int j = 0; j < kChunkCols; ++j)
+                    if (c0 + j < p.ntok) p.ar.own[base + (long long)(c0 + j) * p.ldy] = v[j];
+                } else {
+#pragma unroll
+                  for (int j = 0; j < kChunkCols; ++j)
+                    if (c0 + j < p.ntok) {
+                      const uint16_t h = Elem<T>::from_float(v[j]);
+                      for (int rk = 0; rk < p.ar.world; ++rk)
+                        p.ar.buf[rk][base + (long long)(c0 + j) * p.ldy] = h;
+                    }
+                }
               } else {
 #pragma unroll
                 for (int j = 0; j < kChunkCols; ++j)
@@ -452,17 +467,46 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       __syncwarp();
       named_sync(2, kMmaEpiWarps * 32);
       if (!*ar_fail && kb1 > kb0) {
-        const uint16_t *rb = p.ar.buf[me] + (long long)(ar_epoch & 1u) * W * p.ar.slot_elems;
+        const uint16_t *rb = p.ar.mc ? nullptr : p.ar.buf[me] + (long long)(ar_epoch & 1u) * W * p.ar.slot_elems;
+        const float *mb = p.ar.mc ? p.ar.mc + (long long)(ar_epoch & 1u) * p.ar.slot_elems : nullptr;
+        // All 128 epilogue threads share the CTA's owned (row, feature) elements,
+        // feature fastest, and issue kBatch independent reductions before using
+        // any result, so the latency of the reads overlaps.
+        constexpr int kBatch = 8;
+        const int et = (warp - 2) * 32 + lane;
         for (int j = 0; j < ntiles; ++j) {
-          const int col = tile_box0(j) * kBoxCols + f;
-          const bool col_ok = f < tile_nbox(j) * kBoxCols && col < tier.cols;
-          if (!col_ok || !(ks == 1 || owner == r)) continue;
-          const long long cidx = tier.col_offset + col;
-          for (int row = 0; row < p.ntok; ++row) {
-            const long long idx = (long long)row * p.ldy + cidx;
-            float acc = 0.f;
-            for (int rk = 0; rk < W; ++rk) acc += Elem<T>::to_float(rb[(long long)rk * p.ar.slot_elems + idx]);
-            reinterpret_cast<uint16_t *>(p.y)[idx] = Elem<T>::from_float(acc);
+          const int base_col = tile_box0(j) * kBoxCols;
+          const int f_lo = ks == 1 ? 0 : r * feat_per_owner;
+          int f_hi = ks == 1 ? kMmaBM : f_lo + feat_per_owner;
+          f_hi = min(f_hi, min(tile_nbox(j) * kBoxCols, tier.cols - base_col));
+          const int ncols = f_hi - f_lo;
+          if (ncols <= 0) continue;
+          const long long n = (long long)ncols * p.ntok;
+          const long long cbase = tier.col_offset + base_col + f_lo;
+          for (long long e0 = et; e0 < n; e0 += (long long)kMmaEpiWarps * 32 * kBatch) {
+            long long idx[kBatch];
+            float acc[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+              const long long e = e0 + (long long)u * kMmaEpiWarps * 32;
+              const long long row = e < n ? e / ncols : 0;
+              idx[u] = e < n ? row * p.ldy + cbase + (e - row * ncols) : -1;
+            }
+            if (mb) {
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) acc[u] = idx[u] >= 0 ? multimem_ld_reduce_add(mb + idx[u]) : 0.f;
+            } else {
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) {
+                acc[u] = 0.f;
+                if (idx[u] >= 0)
+                  for (int rk = 0; rk < W; ++rk)
+                    acc[u] += Elem<T>::to_float(rb[(long long)rk * p.ar.slot_elems + idx[u]]);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u)
+              if (idx[u] >= 0) reinterpret_cast<uint16_t *>(p.y)[idx[u]] = Elem<T>::from_float(acc[u]);
           }
         }
       }

@@ -877,13 +877,19 @@ int dak_linear_split_allreduce(const dak_linear_args *args, const dak_allreduce_
     return fail(DAK_ERR_INVALID_ARG, "epoch, done, slot_elems and timeout_us are required");
   ArParams p;
   std::memset(&p, 0, sizeof(p));
+  const bool mc = ar->mc_f32 != nullptr;
+  if (mc != (ar->own_f32 != nullptr)) return fail(DAK_ERR_INVALID_ARG, "own_f32 and mc_f32 come together");
+  if (mc && ((reinterpret_cast<uintptr_t>(ar->own_f32) & 15u) || (reinterpret_cast<uintptr_t>(ar->mc_f32) & 15u)))
+    return fail(DAK_ERR_ALIGNMENT, "own_f32 and mc_f32 must be 16-byte aligned");
   for (int r = 0; r < ar->world; ++r) {
-    if (!ar->buffers[r] || !ar->flags[r]) return fail(DAK_ERR_INVALID_ARG, "rank %d buffer or flags missing", r);
+    if ((!mc && !ar->buffers[r]) || !ar->flags[r]) return fail(DAK_ERR_INVALID_ARG, "rank %d buffer or flags missing", r);
     if ((reinterpret_cast<uintptr_t>(ar->buffers[r]) & 15u) || (reinterpret_cast<uintptr_t>(ar->flags[r]) & 3u))
       return fail(DAK_ERR_ALIGNMENT, "rank %d buffer must be 16-byte aligned, flags 4-byte aligned", r);
     p.buf[r] = static_cast<uint16_t *>(ar->buffers[r]);
     p.flags[r] = ar->flags[r];
   }
+  p.own = ar->own_f32;
+  p.mc = ar->mc_f32;
   p.slot_elems = ar->slot_elems;
   p.epoch = ar->epoch;
   p.done = ar->done;

@@ -112,32 +112,62 @@ def make_offloaded_shard(weight_shard: torch.Tensor, offload_ratio: float, *, ho
 
 class SymmetricAllReduce:
     """Buffers for the all-reduce fused into the linear kernel
-    (``dak_linear_split_allreduce``): a receive buffer of 2 x world slots of
-    ``slot_elems`` 16-bit values and a flag array per rank, in torch symmetric
-    memory (mapped into every rank of ``group``), plus this rank's call
-    counters.  One instance serves any number of sequential calls on one
-    stream; every rank must make the same calls in the same order."""
+    (``dak_linear_split_allreduce``), in torch symmetric memory (mapped into
+    every rank of ``group``), plus this rank's call counters.
+
+    Two modes, chosen collectively: "multimem" when the allocation has a
+    multicast mapping (NVSwitch): each rank keeps its FP32 partials in its own
+    buffer and reads the sum with multimem.ld_reduce; otherwise "peer": each
+    rank pushes its 16-bit partials into every rank's receive slots.  One
+    instance serves any number of sequential calls on one stream; every rank
+    must make the same calls in the same order."""
 
     MAX_CTAS = 1024
 
-    def __init__(self, slot_elems: int, group=None, dtype=torch.float16, timeout_us: int = 2_000_000):
+    def __init__(self, slot_elems: int, group=None, dtype=torch.float16, timeout_us: int = 2_000_000,
+                 multicast: bool = True):
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
+        name = self.group.group_name
         self.rank, self.world = _group_info(self.group)
         if self.world > 8:
             raise ValueError("the fused all-reduce serves at most 8 ranks")
         self.slot_elems = int(slot_elems)
-        self.buf = symm_mem.empty(2 * self.world * self.slot_elems, dtype=dtype, device="cuda")
         self.flags = symm_mem.empty(self.MAX_CTAS * self.world, dtype=torch.int32, device="cuda")
         self.flags.zero_()
+        self.mode, self.own, self.mc = "peer", None, 0
+        if multicast:
+            own = symm_mem.empty(2 * self.slot_elems, dtype=torch.float32, device="cuda")
+            own.zero_()
+            torch.cuda.synchronize()
+            h = symm_mem.rendezvous(own, name)
+            try:
+                has = bool(symm_mem._SymmetricMemory.has_multicast_support(
+                    symm_mem.DeviceType.CUDA, torch.cuda.current_device()))
+            except (AttributeError, TypeError, RuntimeError):
+                has = False
+            ok = torch.tensor([1 if (has and h.multicast_ptr) else 0], dtype=torch.int32, device="cuda")
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+            if int(ok.item()):
+                self.mode, self.own, self._hm = "multimem", own, h
+                self.mc = h.multicast_ptr + (own.data_ptr() - h.buffer_ptrs[self.rank])
+        self.buf = None
+        if self.mode == "peer":
+            self.buf = symm_mem.empty(2 * self.world * self.slot_elems, dtype=dtype, device="cuda")
+            torch.cuda.synchronize()
+            self._hb = symm_mem.rendezvous(self.buf, name)
         torch.cuda.synchronize()
-        self._hb = symm_mem.rendezvous(self.buf, self.group.group_name)
-        self._hf = symm_mem.rendezvous(self.flags, self.group.group_name)
+        self._hf = symm_mem.rendezvous(self.flags, name)
         self.counters = torch.zeros(2, dtype=torch.int32, device="cuda")  # epoch, done
         dist.barrier(group=self.group)
         self.timeout_us = int(timeout_us)
         self._args = None
+
+    @staticmethod
+    def _peer_ptrs(h, t, rank):
+        off = t.data_ptr() - h.buffer_ptrs[rank]
+        return [p + off for p in h.buffer_ptrs]
 
     def args(self, y: torch.Tensor):
         from . import _lib
@@ -147,12 +177,16 @@ class SymmetricAllReduce:
         if self._args is None:
             a = _lib.AllReduceArgs()
             a.world, a.rank = self.world, self.rank
+            flags = self._peer_ptrs(self._hf, self.flags, self.rank)
+            bufs = self._peer_ptrs(self._hb, self.buf, self.rank) if self.mode == "peer" else [0] * self.world
             for r in range(self.world):
-                a.buffers[r] = self._hb.buffer_ptrs[r]
-                a.flags[r] = self._hf.buffer_ptrs[r]
+                a.buffers[r] = bufs[r] or None
+                a.flags[r] = flags[r]
             a.slot_elems = self.slot_elems
             a.epoch = self.counters.data_ptr()
             a.done = self.counters.data_ptr() + 4
             a.timeout_us = self.timeout_us
+            if self.mode == "multimem":
+                a.own_f32, a.mc_f32 = self.own.data_ptr(), self.mc
             self._args = a
         return self._args

@@ -200,7 +200,11 @@ DAK_API int dak_linear_split(const dak_linear_args *args, void *stream);
  *   flags[r]:   rank r's flags, 1024 x world uint32, zero before the first call;
  *   epoch/done: this rank's counters in device memory, zero before the first call.
  * slot_elems >= min(ntok, 256) x ldy.  Stream-ordered, graph-capturable, no
- * allocation; calls on one group must not overlap. */
+ * allocation; calls on one group must not overlap.
+ * Multicast mode (own_f32 and mc_f32 given, e.g. on an NVSwitch box): each rank
+ * stores its FP32 partials in its own buffer own_f32 (2 x slot_elems floats,
+ * mapped into a multicast object whose address is mc_f32), publishes the flags,
+ * and reads the sum over ranks with multimem.ld_reduce; buffers[] are unused. */
 typedef struct dak_allreduce_args {
   int world, rank;
   void *buffers[8];
@@ -208,6 +212,7 @@ typedef struct dak_allreduce_args {
   int64_t slot_elems;
   int *epoch, *done;
   int64_t timeout_us;
+  float *own_f32, *mc_f32;
 } dak_allreduce_args;
 DAK_API int dak_linear_split_allreduce(const dak_linear_args *args, const dak_allreduce_args *ar, void *stream);
 

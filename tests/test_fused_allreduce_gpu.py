@@ -24,7 +24,7 @@ def _rel(a, b):
     return float((a.float() - b.float()).abs().max() / b.float().abs().max())
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, multicast):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -39,7 +39,7 @@ def _worker(rank, world, port, q):
 
         errs = []
         N, Kr = 4096, 1024
-        ar = SymmetricAllReduce(slot_elems=64 * N)
+        ar = SymmetricAllReduce(slot_elems=64 * N, multicast=multicast)
         g = torch.Generator(device="cuda").manual_seed(100 + rank)
         w = (torch.randn(Kr, N, generator=g, device="cuda") * 0.02).half()  # this rank's [K_r, N] shard
         w_host = w[:, :1024].contiguous().cpu().pin_memory()
@@ -71,15 +71,18 @@ def _worker(rank, world, port, q):
                 dist.all_reduce(ref)
                 errs.append(_rel(ys[i], ref))
         del graph
-        q.put((rank, max(errs), runtime.device_status()))
+        q.put((rank, max(errs), runtime.device_status(), ar.mode))
     except Exception as e:  # noqa: BLE001
-        q.put((rank, repr(e), -1))
+        q.put((rank, repr(e), -1, None))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("multicast", [False, True])
 @pytest.mark.parametrize("world", [1, 2])
-def test_fused_allreduce_matches_nccl(world):
+def test_fused_allreduce_matches_nccl(world, multicast):
+    """Peer-store mode, and the multimem mode where the box offers multicast
+    (the context falls back to peer stores otherwise; the mode is reported)."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
@@ -87,15 +90,18 @@ def test_fused_allreduce_matches_nccl(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, multicast)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     for _ in procs:
-        r, err, st = q.get(timeout=600)
-        res[r] = (err, st)
+        r, err, st, mode = q.get(timeout=600)
+        res[r] = (err, st, mode)
     for p in procs:
         p.join(timeout=120)
     for r in range(world):
-        err, st = res[r]
+        err, st, mode = res[r]
         assert isinstance(err, float) and err <= 1e-2 and st == 0, res
+        if not multicast:
+            assert mode == "peer"
+    print("fused all-reduce modes:", {r: res[r][2] for r in res})
