@@ -747,6 +747,7 @@ def run_llama70b(args, torch, rank, world):
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = times.tolist()
     dec.release()
+    dec_ar_mode = dec.ar.mode if dec.ar is not None else None
     if status != 0:
         raise RuntimeError(f"device error word {status} after the timed region")
 
@@ -787,8 +788,8 @@ def run_llama70b(args, torch, rank, world):
                    "host_fraction": round(frac, 4), "per_rank_host_fractions": [round(f, 4) for f in fracs],
                    "rank0_host_bytes": int(lin_host + kv_host),
                    "rank0_device_bytes": int(lin_dev + kv_dev), "build_s": round(build_s, 1),
-                   "parallelism": f"tp{world}", "allreduce": "fused into the o/down kernels over NVLink peer "
-                                                               "memory" if fused else "NCCL",
+                   "parallelism": f"tp{world}",
+                   "allreduce": f"fused into the o/down kernels ({dec_ar_mode})" if fused else "NCCL",
                    "l2": "tens of GB read per step exceed L2",
                    "timing": "CUDA events around K graph replays, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": round((host_step + dev_step) / (step_ms * 1e-3) / 1e9, 2),
