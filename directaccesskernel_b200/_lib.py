@@ -92,7 +92,7 @@ class AllReduceArgs(ctypes.Structure):
     _fields_ = [
         ("world", c_int), ("rank", c_int), ("buffers", c_vp * 8), ("flags", c_vp * 8),
         ("slot_elems", c_i64), ("epoch", c_vp), ("done", c_vp), ("timeout_us", c_i64),
-        ("own_f32", c_vp), ("mc_f32", c_vp),
+        ("own_f32", c_vp), ("mc_f32", c_vp), ("publish_only", c_int),
     ]
 
 
@@ -128,6 +128,8 @@ SIGNATURES = {
     "dak_attn_decode_paged": (c_int, [ctypes.POINTER(AttnPagedArgs), c_vp]),
     "dak_kv_append_paged": (c_int, [ctypes.POINTER(KvAppendArgs), c_vp]),
     "dak_linear_split_allreduce": (c_int, [ctypes.POINTER(LinearArgs), ctypes.POINTER(AllReduceArgs), c_vp]),
+    "dak_rmsnorm_allreduce": (c_int, [ctypes.POINTER(AllReduceArgs), c_vp, c_vp, c_vp, c_int, c_int, c_i64,
+                                      ctypes.c_float, c_int, c_vp]),
     "dak_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_i64, ctypes.c_float, c_int, c_vp]),
     "dak_rope_qk": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp]),
     "dak_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_int, c_int, c_int, c_vp]),

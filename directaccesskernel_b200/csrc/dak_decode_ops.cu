@@ -116,6 +116,80 @@ __global__ void silu_mul_kernel(const void *gu, long long ld, void *out, int row
   }
 }
 
+// RMSNorm whose input is the all-reduce of FP32 partials that every rank of a
+// tensor-parallel group left in its own buffer (dak_linear_split_allreduce in
+// publish-only mode).  Thread 0 waits, bounded, until every rank published the
+// current call; then the row is read as sums over ranks with multimem.ld_reduce
+// through the buffer's multicast address, 8 independent reads per thread at a
+// time.  h = round16(round16(sum) + residual) is written back to the residual
+// stream, and out = w * round16(h * rsqrt(mean(h^2) + eps)).
+__device__ __forceinline__ float mm_ld_reduce_add(const float *p) {
+  float v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_ar_kernel(const float *mc, long long slot, long long ld,
+                                                                  const int *epoch, const uint32_t *flags, int world,
+                                                                  long long timeout_ns, int *status, void *res,
+                                                                  const void *w, void *out, int cols, float eps) {
+  __shared__ int fail_s;
+  __shared__ float red[kNormThreads / 32];
+  const long long row = blockIdx.x;
+  const uint32_t e = (uint32_t)*reinterpret_cast<const volatile int *>(epoch);
+  if (threadIdx.x == 0) {
+    fail_s = 0;
+    const unsigned long long t0 = globaltimer();
+    for (int rk = 0; rk < world && !fail_s; ++rk)
+      while ((int)(ld_acquire_sys_u32(flags + rk) - e) < 0) {
+        if (globaltimer() - t0 > (unsigned long long)timeout_ns) {
+          atomicCAS(status, 0, DAK_ERR_TIMEOUT);
+          fail_s = 1;
+          break;
+        }
+      }
+  }
+  __syncthreads();
+  if (fail_s) return;
+  const float *src = mc + (long long)(e & 1u) * slot + row * ld;
+  uint16_t *rrow = static_cast<uint16_t *>(res) + row * (long long)cols;
+  float ss = 0.f;
+  constexpr int kB = 8;
+  for (int c0 = threadIdx.x; c0 < cols; c0 += kNormThreads * kB) {
+    float v[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int c = c0 + u * kNormThreads;
+      v[u] = c < cols ? mm_ld_reduce_add(src + c) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int c = c0 + u * kNormThreads;
+      if (c < cols) {
+        const float h = r16<T>(r16<T>(v[u]) + ld1<T>(rrow, c));
+        st1<T>(rrow, c, h);
+        ss = fmaf(h, h, ss);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / (float)cols + eps);
+  void *orow = static_cast<uint16_t *>(out) + row * (long long)cols;
+  for (int c = threadIdx.x; c < cols; c += kNormThreads) st1<T>(orow, c, ld1<T>(w, c) * r16<T>(ld1<T>(rrow, c) * inv));
+}
+
 int check_dtype(int dtype) {
   if (dtype != DAK_DTYPE_F16 && dtype != DAK_DTYPE_BF16)
     return fail(DAK_ERR_UNSUPPORTED, "decode ops support float16 and bfloat16");
@@ -180,4 +254,29 @@ extern "C" int dak_silu_mul(const void *gate_up, int64_t ld, void *out, int rows
   else
     silu_mul_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(gate_up, ld, out, rows, cols);
   return cuda_status(cudaGetLastError(), "silu_mul launch");
+}
+
+extern "C" int dak_rmsnorm_allreduce(const dak_allreduce_args *ar, void *residual, const void *weight, void *out,
+                                     int rows, int cols, int64_t ld, float eps, int dtype, void *stream) {
+  using namespace dak;
+  int st = check_dtype(dtype);
+  if (st) return st;
+  if (!ar || !ar->mc_f32 || !ar->epoch || ar->world < 1 || ar->world > 8 || ar->rank < 0 || ar->rank >= ar->world ||
+      !ar->flags[ar->rank])
+    return fail(DAK_ERR_INVALID_ARG, "rmsnorm_allreduce: multicast all-reduce args with this rank's flags are required");
+  if (!residual || !weight || !out || rows <= 0 || cols <= 0 || ld < cols || (long long)rows * ld > ar->slot_elems)
+    return fail(DAK_ERR_INVALID_ARG, "rmsnorm_allreduce: residual, weight, out, rows, cols > 0 and rows x ld <= slot_elems");
+  int *status = device_status_word();
+  if (!status) return fail(DAK_ERR_CUDA, "no device status word");
+  auto s = static_cast<cudaStream_t>(stream);
+  const long long tns = ar->timeout_us * 1000;
+  if (dtype == DAK_DTYPE_F16)
+    rmsnorm_ar_kernel<__half><<<rows, kNormThreads, 0, s>>>(ar->mc_f32, ar->slot_elems, ld, ar->epoch,
+                                                            ar->flags[ar->rank], ar->world, tns, status, residual,
+                                                            weight, out, cols, eps);
+  else
+    rmsnorm_ar_kernel<__nv_bfloat16><<<rows, kNormThreads, 0, s>>>(ar->mc_f32, ar->slot_elems, ld, ar->epoch,
+                                                                   ar->flags[ar->rank], ar->world, tns, status,
+                                                                   residual, weight, out, cols, eps);
+  return cuda_status(cudaGetLastError(), "rmsnorm_allreduce launch");
 }

@@ -91,6 +91,8 @@ struct ArParams {
   int *done;                     // this rank's finished-CTA counter
   int world, rank;
   long long timeout_ns;
+  int publish_only;              // multicast mode: store and publish; the consumer reduces
+  int pad_;
 };
 
 struct alignas(64) LinearParams {

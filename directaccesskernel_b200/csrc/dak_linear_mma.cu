@@ -445,7 +445,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         if (lane == 0) mbar_arrive(tempty0 + 8 * ab);
       }
     }
-    if (AR) {
+    if (AR && p.ar.publish_only) {
+      // ---- publish only: the partials stay in this rank's buffer; the last
+      // CTA to finish tells every rank that call e is complete, and the
+      // consumer kernel (dak_rmsnorm_allreduce) reads the sum over ranks.
+      __threadfence_system();
+      named_sync(2, kMmaEpiWarps * 32);
+      if (warp == 2 && lane == 0) {
+        __threadfence_system();
+        if (atomicAdd(p.ar.done, 1) == (int)gridDim.x - 1) {
+          *p.ar.done = 0;
+          __threadfence_system();
+          for (int rk = 0; rk < p.ar.world; ++rk) st_release_sys(p.ar.flags[rk] + p.ar.rank, ar_epoch);
+          atomicExch(p.ar.epoch, (int)ar_epoch);
+        }
+      }
+      __syncwarp();
+    } else if (AR) {
       // ---- fused all-reduce: publish, wait for every rank's same CTA, sum
       const int W = p.ar.world, me = p.ar.rank, c = (int)blockIdx.x;
       volatile int *ar_fail = abort_flag + 2;

@@ -890,6 +890,8 @@ int dak_linear_split_allreduce(const dak_linear_args *args, const dak_allreduce_
   }
   p.own = ar->own_f32;
   p.mc = ar->mc_f32;
+  if (ar->publish_only && !mc) return fail(DAK_ERR_INVALID_ARG, "publish_only needs the multicast buffers");
+  p.publish_only = ar->publish_only ? 1 : 0;
   p.slot_elems = ar->slot_elems;
   p.epoch = ar->epoch;
   p.done = ar->done;

@@ -130,7 +130,7 @@ class TPLlamaDecoder(nn.Module):
         if fused_allreduce:
             from .tp import SymmetricAllReduce
 
-            self.ar = SymmetricAllReduce(batch * shape.hidden, group=group, dtype=dtype)
+            self.ar = SymmetricAllReduce(batch * shape.hidden, group=group, dtype=dtype, consumer_reduces=True)
 
     # ------------------------------------------------------------- weights
     def _make_linear(self, w: torch.Tensor) -> nn.Module:
@@ -281,6 +281,15 @@ class TPLlamaDecoder(nn.Module):
         if self.world > 1:
             dist.all_reduce(t, group=self.group)
 
+    def _add_norm(self, y: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """hidden += y (summed over ranks); returns RMSNorm(hidden) * w.  In
+        publish-only mode the sum over ranks is read here, inside the norm."""
+        from .decode_ops import rmsnorm
+
+        if self.ar is not None and self.ar.publish_only:
+            return self.ar.rmsnorm(y, self.hidden, w, self.s.eps, self.x_buf)
+        return rmsnorm(y, w, self.s.eps, residual=self.hidden, out=self.x_buf)
+
     def _row_parallel(self, mod: nn.Module, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """A row-parallel projection summed over the ranks: the fused kernel when
         enabled, else the local linear followed by an NCCL all-reduce."""
@@ -319,11 +328,11 @@ class TPLlamaDecoder(nn.Module):
                          out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
                          max_seq_len=self.max_ctx)
             o = self._row_parallel(layer.o, self.attn_out.view(B, qd), self.o_buf)
-            x = rmsnorm(o, layer.post_w, s.eps, residual=self.hidden, out=self.x_buf)
+            x = self._add_norm(o, layer.post_w)
             gu = layer.gate_up(x)
             dn = self._row_parallel(layer.down, silu_mul(gu, out=self.act_buf), self.dn_buf)
             nxt_w = self.layers[l + 1].in_w if l + 1 < len(self.layers) else self.final_w
-            x = rmsnorm(dn, nxt_w, s.eps, residual=self.hidden, out=self.x_buf)
+            x = self._add_norm(dn, nxt_w)
         logits = self.lm_head(x)[:, :max(1, self.vocab_valid)]
         val, idx = logits.float().max(dim=-1)
         if self.world > 1:

@@ -125,7 +125,7 @@ class SymmetricAllReduce:
     MAX_CTAS = 1024
 
     def __init__(self, slot_elems: int, group=None, dtype=torch.float16, timeout_us: int = 2_000_000,
-                 multicast: bool = True):
+                 multicast: bool = True, consumer_reduces: bool = False):
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -162,6 +162,9 @@ class SymmetricAllReduce:
         self.counters = torch.zeros(2, dtype=torch.int32, device="cuda")  # epoch, done
         dist.barrier(group=self.group)
         self.timeout_us = int(timeout_us)
+        # Publish-only (multimem mode): the linear kernel leaves its partials in
+        # place and the consumer, ``rmsnorm``, reads their sum.
+        self.publish_only = bool(consumer_reduces and self.mode == "multimem")
         self._args = None
 
     @staticmethod
@@ -188,5 +191,24 @@ class SymmetricAllReduce:
             a.timeout_us = self.timeout_us
             if self.mode == "multimem":
                 a.own_f32, a.mc_f32 = self.own.data_ptr(), self.mc
+            a.publish_only = 1 if self.publish_only else 0
             self._args = a
         return self._args
+
+    def rmsnorm(self, y: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                out: torch.Tensor) -> torch.Tensor:
+        """After a publish-only linear call that targeted ``y`` (not written): residual
+        += the sum over ranks (rounded to 16 bit), out = RMSNorm(residual) * weight."""
+        from ._lib import LIB, check
+        from .runtime import dak_dtype
+
+        if not self.publish_only:
+            raise RuntimeError("rmsnorm of the all-reduce needs the publish-only (multimem) mode")
+        rows, cols = residual.shape
+        if not (residual.is_contiguous() and out.is_contiguous() and weight.numel() == cols):
+            raise RuntimeError("residual and out must be contiguous [rows, cols], weight [cols]")
+        check(LIB.dak_rmsnorm_allreduce(__import__("ctypes").byref(self.args(y)), residual.data_ptr(),
+                                        weight.data_ptr(), out.data_ptr(), rows, cols, y.stride(0), float(eps),
+                                        dak_dtype(residual.dtype), torch.cuda.current_stream().cuda_stream),
+              "rmsnorm_allreduce")
+        return out

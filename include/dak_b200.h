@@ -213,8 +213,19 @@ typedef struct dak_allreduce_args {
   int *epoch, *done;
   int64_t timeout_us;
   float *own_f32, *mc_f32;
+  int publish_only;   /* multicast mode only: store and publish; dak_rmsnorm_allreduce reduces */
 } dak_allreduce_args;
 DAK_API int dak_linear_split_allreduce(const dak_linear_args *args, const dak_allreduce_args *ar, void *stream);
+
+/* The consumer side of publish-only mode (no reference counterpart): RMSNorm
+ * whose input is the sum over ranks of the FP32 partials that the preceding
+ * dak_linear_split_allreduce (publish_only = 1, same args) left in every rank's
+ * buffer.  Waits, bounded, for every rank to publish the call; reads the sums
+ * with multimem.ld_reduce; residual [rows, cols] (contiguous) is updated in
+ * place to round16(round16(sum) + residual); out [rows, cols] receives the
+ * normalised row.  ld is the row stride the linear used for its output. */
+DAK_API int dak_rmsnorm_allreduce(const dak_allreduce_args *ar, void *residual, const void *weight, void *out,
+                                  int rows, int cols, int64_t ld, float eps, int dtype, void *stream);
 
 /* flush_l2_cache (src/torch_runtime.cu:363-371; include/task/utils.cuh:3-14):
  * reads n floats of `dummy` past L2 and folds them into *sink. */

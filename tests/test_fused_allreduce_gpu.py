@@ -105,3 +105,73 @@ def test_fused_allreduce_matches_nccl(world, multicast):
         if not multicast:
             assert mode == "peer"
     print("fused all-reduce modes:", {r: res[r][2] for r in res})
+
+
+def _consumer_worker(rank, world, port, q):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from directaccesskernel_b200 import runtime
+        from directaccesskernel_b200.tp import SymmetricAllReduce
+
+        N, Kr = 4096, 1024
+        ar = SymmetricAllReduce(slot_elems=64 * N, consumer_reduces=True)
+        if not ar.publish_only:
+            q.put((rank, "no multicast", 0, ar.mode))
+            return
+        g = torch.Generator(device="cuda").manual_seed(200 + rank)
+        gs = torch.Generator(device="cuda").manual_seed(7)  # same residual and weight on every rank
+        w = (torch.randn(Kr, N, generator=g, device="cuda") * 0.02).half()
+        w_host, w_dev = w[:, :512].contiguous().cpu().pin_memory(), w[:, 512:].contiguous()
+        errs = []
+        for ntok in (1, 32, 5, 32):
+            x = torch.randn(ntok, Kr, generator=g, device="cuda").half()
+            res = torch.randn(ntok, N, generator=gs, device="cuda").half()
+            wn = (1 + 0.1 * torch.randn(N, generator=gs, device="cuda")).half()
+            y = torch.empty(ntok, N, dtype=torch.float16, device="cuda")  # layout only: not written
+            runtime.linear_split(x, y, w_host, w_dev, allreduce=ar)
+            state, out = res.clone(), torch.empty_like(res)
+            ar.rmsnorm(y, state, wn, 1e-5, out)
+            ref = (x.float() @ w.float()).contiguous()
+            dist.all_reduce(ref)
+            h = ref.half() + res
+            hf = h.float()
+            out_ref = wn * (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)).half()
+            errs += [_rel(state, h), _rel(out, out_ref)]
+        q.put((rank, max(errs), runtime.device_status(), ar.mode))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e), -1, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_consumer_side_reduction_in_rmsnorm():
+    """Publish-only linear + dak_rmsnorm_allreduce against linear + NCCL all-reduce
+    + residual add + RMSNorm; needs 2 GPUs with NVSwitch multicast."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_consumer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, err, st, mode = q.get(timeout=600)
+        res[r] = (err, st, mode)
+    for p in procs:
+        p.join(timeout=120)
+    if all(v[0] == "no multicast" for v in res.values()):
+        pytest.skip("no NVSwitch multicast on this box")
+    for r in range(2):
+        err, st, mode = res[r]
+        assert isinstance(err, float) and err <= 1e-2 and st == 0, res
