@@ -134,14 +134,31 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
   return v;
 }
 
+// One row is split over a cluster of kArCluster CTAs, so that every read of the
+// row through the switch is in flight at once: each CTA handles cols /
+// kArCluster columns with one batch of independent reads per thread, and the
+// CTAs' sums of squares meet through distributed shared memory.
+constexpr int kArCluster = 8;
+constexpr int kArThreads = 128;
+constexpr int kArPerThread = 8;  // columns per thread: cols <= kArCluster x 128 x 8 = 8192
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_ar_kernel(const float *mc, long long slot, long long ld,
-                                                                  const int *epoch, const uint32_t *flags, int world,
-                                                                  long long timeout_ns, int *status, void *res,
-                                                                  const void *w, void *out, int cols, float eps) {
+__global__ void __launch_bounds__(kArThreads) rmsnorm_ar_kernel(const float *mc, long long slot, long long ld,
+                                                                const int *epoch, const uint32_t *flags, int world,
+                                                                long long timeout_ns, int *status, void *res,
+                                                                const void *w, void *out, int cols, float eps) {
   __shared__ int fail_s;
-  __shared__ float red[kNormThreads / 32];
-  const long long row = blockIdx.x;
+  __shared__ float red[kArThreads / 32];
+  __shared__ float part;  // this CTA's sum of squares, read by the cluster
+  const int k = (int)cluster_ctarank();
+  const long long row = blockIdx.x / kArCluster;
+  const int c_lo = (int)((long long)k * cols / kArCluster), c_hi = (int)((long long)(k + 1) * cols / kArCluster);
   const uint32_t e = (uint32_t)*reinterpret_cast<const volatile int *>(epoch);
   if (threadIdx.x == 0) {
     fail_s = 0;
@@ -156,38 +173,51 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_ar_kernel(const float *m
       }
   }
   __syncthreads();
-  if (fail_s) return;
+  const bool ok = !fail_s;
   const float *src = mc + (long long)(e & 1u) * slot + row * ld;
   uint16_t *rrow = static_cast<uint16_t *>(res) + row * (long long)cols;
+  float v[kArPerThread];
+#pragma unroll
+  for (int u = 0; u < kArPerThread; ++u) {
+    const int c = c_lo + threadIdx.x + u * kArThreads;
+    v[u] = (ok && c < c_hi) ? mm_ld_reduce_add(src + c) : 0.f;
+  }
   float ss = 0.f;
-  constexpr int kB = 8;
-  for (int c0 = threadIdx.x; c0 < cols; c0 += kNormThreads * kB) {
-    float v[kB];
 #pragma unroll
-    for (int u = 0; u < kB; ++u) {
-      const int c = c0 + u * kNormThreads;
-      v[u] = c < cols ? mm_ld_reduce_add(src + c) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < kB; ++u) {
-      const int c = c0 + u * kNormThreads;
-      if (c < cols) {
-        const float h = r16<T>(r16<T>(v[u]) + ld1<T>(rrow, c));
-        st1<T>(rrow, c, h);
-        ss = fmaf(h, h, ss);
-      }
+  for (int u = 0; u < kArPerThread; ++u) {
+    const int c = c_lo + threadIdx.x + u * kArThreads;
+    if (ok && c < c_hi) {
+      const float h = r16<T>(r16<T>(v[u]) + ld1<T>(rrow, c));
+      v[u] = h;
+      st1<T>(rrow, c, h);
+      ss = fmaf(h, h, ss);
     }
   }
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kArThreads / 32; ++i) t += red[i];
+    part = t;
+  }
+  // Every CTA's partial is written before any CTA reads them, and no CTA
+  // leaves while a peer may still read its shared memory.
+  cluster_sync_all();
   float tot = 0.f;
 #pragma unroll
-  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  for (int q = 0; q < kArCluster; ++q) tot += ld_cluster_f32(mapa_shared(smem_u32(&part), (uint32_t)q));
+  cluster_sync_all();
+  if (!ok) return;
   const float inv = rsqrtf(tot / (float)cols + eps);
-  void *orow = static_cast<uint16_t *>(out) + row * (long long)cols;
-  for (int c = threadIdx.x; c < cols; c += kNormThreads) st1<T>(orow, c, ld1<T>(w, c) * r16<T>(ld1<T>(rrow, c) * inv));
+  uint16_t *orow = static_cast<uint16_t *>(out) + row * (long long)cols;
+#pragma unroll
+  for (int u = 0; u < kArPerThread; ++u) {
+    const int c = c_lo + threadIdx.x + u * kArThreads;
+    if (c < c_hi) st1<T>(orow, c, ld1<T>(w, c) * r16<T>(v[u] * inv));
+  }
 }
 
 int check_dtype(int dtype) {
@@ -270,13 +300,29 @@ extern "C" int dak_rmsnorm_allreduce(const dak_allreduce_args *ar, void *residua
   if (!status) return fail(DAK_ERR_CUDA, "no device status word");
   auto s = static_cast<cudaStream_t>(stream);
   const long long tns = ar->timeout_us * 1000;
+  if (cols > kArCluster * kArThreads * kArPerThread)
+    return fail(DAK_ERR_UNSUPPORTED, "rmsnorm_allreduce serves at most %d columns", kArCluster * kArThreads * kArPerThread);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows * kArCluster);
+  cfg.blockDim = dim3(kArThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kArCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (dtype == DAK_DTYPE_F16)
-    rmsnorm_ar_kernel<__half><<<rows, kNormThreads, 0, s>>>(ar->mc_f32, ar->slot_elems, ld, ar->epoch,
-                                                            ar->flags[ar->rank], ar->world, tns, status, residual,
-                                                            weight, out, cols, eps);
+    e = cudaLaunchKernelEx(&cfg, rmsnorm_ar_kernel<__half>, (const float *)ar->mc_f32, (long long)ar->slot_elems,
+                           (long long)ld, (const int *)ar->epoch, (const uint32_t *)ar->flags[ar->rank], ar->world, tns,
+                           status, residual, weight, out, cols, eps);
   else
-    rmsnorm_ar_kernel<__nv_bfloat16><<<rows, kNormThreads, 0, s>>>(ar->mc_f32, ar->slot_elems, ld, ar->epoch,
-                                                                   ar->flags[ar->rank], ar->world, tns, status,
-                                                                   residual, weight, out, cols, eps);
+    e = cudaLaunchKernelEx(&cfg, rmsnorm_ar_kernel<__nv_bfloat16>, (const float *)ar->mc_f32,
+                           (long long)ar->slot_elems, (long long)ld, (const int *)ar->epoch,
+                           (const uint32_t *)ar->flags[ar->rank], ar->world, tns, status, residual, weight, out, cols,
+                           eps);
+  if (e != cudaSuccess) return cuda_status(e, "rmsnorm_allreduce launch");
   return cuda_status(cudaGetLastError(), "rmsnorm_allreduce launch");
 }

@@ -223,7 +223,8 @@ DAK_API int dak_linear_split_allreduce(const dak_linear_args *args, const dak_al
  * buffer.  Waits, bounded, for every rank to publish the call; reads the sums
  * with multimem.ld_reduce; residual [rows, cols] (contiguous) is updated in
  * place to round16(round16(sum) + residual); out [rows, cols] receives the
- * normalised row.  ld is the row stride the linear used for its output. */
+ * normalised row.  ld is the row stride the linear used for its output.  Each
+ * row is split over a cluster of 8 CTAs (cols <= 8192). */
 DAK_API int dak_rmsnorm_allreduce(const dak_allreduce_args *ar, void *residual, const void *weight, void *out,
                                   int rows, int cols, int64_t ld, float eps, int dtype, void *stream);
 
