@@ -58,8 +58,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
     ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
     ap.add_argument("--ctx", type=int, default=16384, help="llama70b: context tokens per sequence")
-    ap.add_argument("--fused-allreduce", action="store_true",
-                    help="llama70b: all-reduce of o and down fused into their kernels (default: NCCL)")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="llama70b: NCCL all-reduce after o and down instead of the fused path")
     ap.add_argument("--no-balance", action="store_true",
                     help="llama70b: same host fraction on every rank (default: balanced by host bandwidth)")
     ap.add_argument("--host-fraction", type=float, default=None,
@@ -703,7 +703,7 @@ def run_llama70b(args, torch, rank, world):
         raise SystemExit(f"llama70b at TP{world}: {host_need / 1e9:.0f} GB of pinned host memory needed, more than "
                          f"3/4 of the box's {ram / 1e9:.0f} GB; use --layers / --host-fraction")
     t0 = time.perf_counter()
-    fused = world > 1 and args.fused_allreduce
+    fused = world > 1 and not args.nccl_allreduce
     dec = TPLlamaDecoder(shape, batch=B, max_ctx=max_ctx, weight_offload=my_frac, kv_host_fraction=my_frac,
                          fused_allreduce=fused)
     dec.init_random(seed=0)
@@ -748,6 +748,7 @@ def run_llama70b(args, torch, rank, world):
     ms, e2e_ms = times.tolist()
     dec.release()
     dec_ar_mode = dec.ar.mode if dec.ar is not None else None
+    fused = fused and dec_ar_mode is not None
     if status != 0:
         raise RuntimeError(f"device error word {status} after the timed region")
 
@@ -789,7 +790,8 @@ def run_llama70b(args, torch, rank, world):
                    "rank0_host_bytes": int(lin_host + kv_host),
                    "rank0_device_bytes": int(lin_dev + kv_dev), "build_s": round(build_s, 1),
                    "parallelism": f"tp{world}",
-                   "allreduce": f"fused into the o/down kernels ({dec_ar_mode})" if fused else "NCCL",
+                   "allreduce": "fused: row-parallel kernels publish, the next RMSNorm reduces over NVSwitch "
+                                "multicast" if fused else "NCCL",
                    "l2": "tens of GB read per step exceed L2",
                    "timing": "CUDA events around K graph replays, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": round((host_step + dev_step) / (step_ms * 1e-3) / 1e9, 2),

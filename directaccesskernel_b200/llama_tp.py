@@ -124,13 +124,16 @@ class TPLlamaDecoder(nn.Module):
         self._alloc_kv()
         self._alloc_buffers()
         self.graph = None
-        # o and down with their all-reduce fused into the linear kernel (peer
-        # memory over NVLink) instead of a separate NCCL all-reduce.
+        # o and down with their all-reduce fused: the row-parallel kernel leaves
+        # its partial in place and the RMSNorm that follows reads the sum over
+        # ranks through the NVSwitch multicast mapping.  Without multicast the
+        # decoder keeps the NCCL all-reduce (measured faster than peer pushes).
         self.ar = None
-        if fused_allreduce:
+        if fused_allreduce and self.world > 1:
             from .tp import SymmetricAllReduce
 
-            self.ar = SymmetricAllReduce(batch * shape.hidden, group=group, dtype=dtype, consumer_reduces=True)
+            ar = SymmetricAllReduce(batch * shape.hidden, group=group, dtype=dtype, consumer_reduces=True)
+            self.ar = ar if ar.publish_only else None
 
     # ------------------------------------------------------------- weights
     def _make_linear(self, w: torch.Tensor) -> nn.Module:
