@@ -20,6 +20,15 @@ int *device_status_word();
 // DAK_OK if `p` is memory of the current device or pinned host memory.
 int check_gpu_accessible(const void *p, const char *what);
 
+// Shared memory one linear-kernel CTA may fill with pipeline stages, in bytes.
+// All of it (227 KB) by default.  DAK_B200_SMEM_BUDGET_KB lowers it (not below
+// 64 KB) so that two CTAs fit on one SM: under programmatic dependent launch
+// the next layer's CTAs then stream their first weight stages while this
+// layer's last tiles finish.  A layout keeps at least two stages whatever the
+// budget, and the tcgen05 kernel only follows it while two CTAs' TMEM columns
+// fit in one SM.
+uint32_t linear_smem_budget();
+
 // Shared-memory bytes and launch of the CUDA-core kernel for `ntok_tmpl`
 // (1, 2, 4 or 8) tokens and dtype (DAK_DTYPE_F16 / _BF16).  With grid == 0
 // nothing is launched and *max_clusters (if given) receives how many

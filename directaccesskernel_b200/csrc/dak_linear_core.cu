@@ -59,7 +59,8 @@ struct CoreLayout {
   }
   static int stages_for(int red_slots) {
     int s = kCoreStages;
-    while (s > 2 && CoreLayout(s).bytes(red_slots) > kCoreSmemBudget) --s;
+    const uint32_t budget = std::min(kCoreSmemBudget, linear_smem_budget());
+    while (s > 2 && CoreLayout(s).bytes(red_slots) > budget) --s;
     return s;
   }
 };

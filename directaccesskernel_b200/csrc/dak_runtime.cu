@@ -302,6 +302,18 @@ int desc_to_matrix(const void *blob, const char *what, MatView *out) {
 }
 }  // namespace
 
+uint32_t linear_smem_budget() {
+  static const uint32_t bytes = [] {
+    const uint32_t full = 227u * 1024u;
+    const char *v = getenv("DAK_B200_SMEM_BUDGET_KB");
+    if (!v || !v[0]) return full;
+    const long kb = strtol(v, nullptr, 10);
+    if (kb <= 0) return full;
+    return (uint32_t)std::min<long>(227, std::max<long>(64, kb)) * 1024u;
+  }();
+  return bytes;
+}
+
 // ---------------------------------------------------------- the split linear
 namespace {
 constexpr int kAutoHostCtas = 8;  // two CTAs with 4 x 32 KB in flight already saturate PCIe Gen5

@@ -16,6 +16,8 @@ collectives run on the current stream after the local kernel.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 from torch import nn
@@ -207,7 +209,7 @@ class SymmetricAllReduce:
         rows, cols = residual.shape
         if not (residual.is_contiguous() and out.is_contiguous() and weight.numel() == cols):
             raise RuntimeError("residual and out must be contiguous [rows, cols], weight [cols]")
-        check(LIB.dak_rmsnorm_allreduce(__import__("ctypes").byref(self.args(y)), residual.data_ptr(),
+        check(LIB.dak_rmsnorm_allreduce(ctypes.byref(self.args(y)), residual.data_ptr(),
                                         weight.data_ptr(), out.data_ptr(), rows, cols, y.stride(0), float(eps),
                                         dak_dtype(residual.dtype), torch.cuda.current_stream().cuda_stream),
               "rmsnorm_allreduce")
