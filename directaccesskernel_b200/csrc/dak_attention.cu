@@ -55,6 +55,7 @@ struct alignas(64) AttnParams {
   int batch, host_size, num_q_heads, num_kv_heads, seq_len, split_size, num_splits, page_size;
   float scaling;
   int *status;
+  int pdl;                 // launched with programmatic stream serialization
 };
 
 struct AttnSmem {
@@ -138,6 +139,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
   uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
   const uint32_t sbase = smem_u32(smem);
   using S = AttnSmem;
+  pdl_enter(p.pdl);  // q, the newest K/V and seq_lens come from the kernels before
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -415,6 +417,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
 // Log-sum-exp merge of the splits (opt_attention_kernel.cuh:362-386).
 template <typename T>
 __global__ void __launch_bounds__(kHeadDim) attn_merge_kernel(const __grid_constant__ AttnParams p) {
+  pdl_enter(p.pdl);
   const int hq = blockIdx.x % p.num_q_heads;
   const int b = blockIdx.x / p.num_q_heads;
   const int d = threadIdx.x;
@@ -439,11 +442,9 @@ cudaError_t launch_g(const AttnParams &p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AttnSmem::bytes);
   if (e != cudaSuccess) return e;
   const int grid = p.batch * p.num_kv_heads * p.num_splits;
-  kern<<<grid, kAttnThreads, AttnSmem::bytes, stream>>>(p);
-  e = cudaGetLastError();
+  e = launch_ex(kern, dim3(grid), dim3(kAttnThreads), AttnSmem::bytes, stream, 1, p.pdl != 0, p);
   if (e != cudaSuccess || p.num_splits == 1) return e;
-  attn_merge_kernel<T><<<p.batch * p.num_q_heads, kHeadDim, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_ex(attn_merge_kernel<T>, dim3(p.batch * p.num_q_heads), dim3(kHeadDim), 0, stream, 1, p.pdl != 0, p);
 }
 
 template <typename T>
@@ -549,6 +550,7 @@ int dak_attn_decode(const dak_attn_decode_args *a, void *stream) {
   const int gpu_batch = a->batch - a->host_size;
   AttnParams p;
   std::memset(&p, 0, sizeof(p));
+  p.pdl = decode_pdl_enabled() ? 1 : 0;
   if (gpu_batch > 0) {
     if ((st = check_kv_strides(a->key, a->kv_stride_b, a->kv_stride_h, "key"))) return st;
     if ((st = check_kv_strides(a->value, a->kv_stride_b, a->kv_stride_h, "value"))) return st;
@@ -612,6 +614,7 @@ int dak_attn_decode_paged(const dak_attn_paged_args *a, void *stream) {
   if (!a->query || !a->out) return fail(DAK_ERR_INVALID_ARG, "query and out are required");
   AttnParams p;
   std::memset(&p, 0, sizeof(p));
+  p.pdl = decode_pdl_enabled() ? 1 : 0;
   const long long hs = (long long)a->page_size * kHeadDim;      // head stride in a page
   const long long ps = hs * a->num_kv_heads;                     // page stride
   // The pools' page counts are not passed; the maps cover the largest page

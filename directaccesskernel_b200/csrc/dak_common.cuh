@@ -238,6 +238,17 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Entry of a decode-step kernel (norms, rotary, SiLU-gate, KV append,
+// attention, merge): when launched with programmatic stream serialization
+// (`pdl` set), every thread waits for the previous kernel of the stream before
+// touching memory, and the next kernel may then be scheduled.
+__device__ __forceinline__ void pdl_enter(int pdl) {
+  if (pdl) {
+    griddep_wait();
+    griddep_launch_dependents();
+  }
+}
+
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 

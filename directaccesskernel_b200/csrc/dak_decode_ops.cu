@@ -33,7 +33,9 @@ constexpr int kNormThreads = 256;
 // rsqrt(mean(h^2) + eps)) with the statistics in FP32 (transformers LlamaRMSNorm).
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const void *x, const void *res, const void *w, void *out,
-                                                               void *res_out, int cols, long long ld, float eps) {
+                                                               void *res_out, int cols, long long ld, float eps,
+                                                               int pdl) {
+  pdl_enter(pdl);
   const long long row = blockIdx.x;
   const void *xr = static_cast<const uint16_t *>(x) + row * ld;
   const void *rr = res ? static_cast<const uint16_t *>(res) + row * ld : nullptr;
@@ -68,7 +70,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const void *x, co
 // embedding); v heads are copied, so all three outputs are contiguous.
 template <typename T>
 __global__ void rope_qk_kernel(const void *qkv, long long ld, const int32_t *pos, const float *inv_freq, void *q_out,
-                               void *k_out, void *v_out, int q_heads, int kv_heads, int d) {
+                               void *k_out, void *v_out, int q_heads, int kv_heads, int d, int pdl) {
+  pdl_enter(pdl);
   const int heads = q_heads + 2 * kv_heads;
   const int b = blockIdx.x / heads;
   const int hh = blockIdx.x - b * heads;
@@ -104,7 +107,8 @@ __global__ void rope_qk_kernel(const void *qkv, long long ld, const int32_t *pos
 
 // out[r, c] = round16(silu(g)) * u with g = gu[r, c], u = gu[r, cols + c].
 template <typename T>
-__global__ void silu_mul_kernel(const void *gu, long long ld, void *out, int rows, int cols) {
+__global__ void silu_mul_kernel(const void *gu, long long ld, void *out, int rows, int cols, int pdl) {
+  pdl_enter(pdl);
   const long long n = (long long)rows * cols;
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
     const long long r = e / cols;
@@ -152,7 +156,9 @@ template <typename T>
 __global__ void __launch_bounds__(kArThreads) rmsnorm_ar_kernel(const float *mc, long long slot, long long ld,
                                                                 const int *epoch, const uint32_t *flags, int world,
                                                                 long long timeout_ns, int *status, void *res,
-                                                                const void *w, void *out, int cols, float eps) {
+                                                                const void *w, void *out, int cols, float eps,
+                                                                int pdl) {
+  pdl_enter(pdl);  // the epoch below is advanced by the linear kernel before this one
   __shared__ int fail_s;
   __shared__ float red[kArThreads / 32];
   __shared__ float part;  // this CTA's sum of squares, read by the cluster
@@ -239,11 +245,14 @@ extern "C" int dak_rmsnorm(const void *x, const void *residual, const void *weig
   if ((residual == nullptr) != (residual_out == nullptr))
     return fail(DAK_ERR_INVALID_ARG, "rmsnorm: residual and residual_out come together");
   auto s = static_cast<cudaStream_t>(stream);
-  if (dtype == DAK_DTYPE_F16)
-    rmsnorm_kernel<__half><<<rows, kNormThreads, 0, s>>>(x, residual, weight, out, residual_out, cols, ld, eps);
-  else
-    rmsnorm_kernel<__nv_bfloat16><<<rows, kNormThreads, 0, s>>>(x, residual, weight, out, residual_out, cols, ld, eps);
-  return cuda_status(cudaGetLastError(), "rmsnorm launch");
+  const int pdl = decode_pdl_enabled() ? 1 : 0;
+  const cudaError_t e =
+      dtype == DAK_DTYPE_F16
+          ? launch_ex(rmsnorm_kernel<__half>, dim3(rows), dim3(kNormThreads), 0, s, 1, pdl, x, residual, weight, out,
+                      residual_out, cols, (long long)ld, eps, pdl)
+          : launch_ex(rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), 0, s, 1, pdl, x, residual, weight,
+                      out, residual_out, cols, (long long)ld, eps, pdl);
+  return cuda_status(e, "rmsnorm launch");
 }
 
 extern "C" int dak_rope_qk(const void *qkv, int64_t ld, const int32_t *positions, const float *inv_freq, void *q_out,
@@ -261,13 +270,14 @@ extern "C" int dak_rope_qk(const void *qkv, int64_t ld, const int32_t *positions
   auto s = static_cast<cudaStream_t>(stream);
   const int grid = batch * (q_heads + 2 * kv_heads);
   const int threads = ((head_dim / 2 + 31) / 32) * 32;
-  if (dtype == DAK_DTYPE_F16)
-    rope_qk_kernel<__half><<<grid, threads, 0, s>>>(qkv, ld, positions, inv_freq, q_out, k_out, v_out, q_heads,
-                                                    kv_heads, head_dim);
-  else
-    rope_qk_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(qkv, ld, positions, inv_freq, q_out, k_out, v_out,
-                                                           q_heads, kv_heads, head_dim);
-  return cuda_status(cudaGetLastError(), "rope_qk launch");
+  const int pdl = decode_pdl_enabled() ? 1 : 0;
+  const cudaError_t e =
+      dtype == DAK_DTYPE_F16
+          ? launch_ex(rope_qk_kernel<__half>, dim3(grid), dim3(threads), 0, s, 1, pdl, qkv, (long long)ld, positions,
+                      inv_freq, q_out, k_out, v_out, q_heads, kv_heads, head_dim, pdl)
+          : launch_ex(rope_qk_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, s, 1, pdl, qkv, (long long)ld,
+                      positions, inv_freq, q_out, k_out, v_out, q_heads, kv_heads, head_dim, pdl);
+  return cuda_status(e, "rope_qk launch");
 }
 
 extern "C" int dak_silu_mul(const void *gate_up, int64_t ld, void *out, int rows, int cols, int dtype, void *stream) {
@@ -279,11 +289,14 @@ extern "C" int dak_silu_mul(const void *gate_up, int64_t ld, void *out, int rows
   auto s = static_cast<cudaStream_t>(stream);
   const long long n = (long long)rows * cols;
   const int grid = (int)std::min<long long>((n + 255) / 256, 148 * 8);
-  if (dtype == DAK_DTYPE_F16)
-    silu_mul_kernel<__half><<<grid, 256, 0, s>>>(gate_up, ld, out, rows, cols);
-  else
-    silu_mul_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(gate_up, ld, out, rows, cols);
-  return cuda_status(cudaGetLastError(), "silu_mul launch");
+  const int pdl = decode_pdl_enabled() ? 1 : 0;
+  const cudaError_t e =
+      dtype == DAK_DTYPE_F16
+          ? launch_ex(silu_mul_kernel<__half>, dim3(grid), dim3(256), 0, s, 1, pdl, gate_up, (long long)ld, out, rows,
+                      cols, pdl)
+          : launch_ex(silu_mul_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, 1, pdl, gate_up, (long long)ld,
+                      out, rows, cols, pdl);
+  return cuda_status(e, "silu_mul launch");
 }
 
 extern "C" int dak_rmsnorm_allreduce(const dak_allreduce_args *ar, void *residual, const void *weight, void *out,
@@ -302,27 +315,17 @@ extern "C" int dak_rmsnorm_allreduce(const dak_allreduce_args *ar, void *residua
   const long long tns = ar->timeout_us * 1000;
   if (cols > kArCluster * kArThreads * kArPerThread)
     return fail(DAK_ERR_UNSUPPORTED, "rmsnorm_allreduce serves at most %d columns", kArCluster * kArThreads * kArPerThread);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)rows * kArCluster);
-  cfg.blockDim = dim3(kArThreads);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kArCluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  const int pdl = decode_pdl_enabled() ? 1 : 0;
+  const dim3 grid((unsigned)rows * kArCluster), block(kArThreads);
   cudaError_t e;
   if (dtype == DAK_DTYPE_F16)
-    e = cudaLaunchKernelEx(&cfg, rmsnorm_ar_kernel<__half>, (const float *)ar->mc_f32, (long long)ar->slot_elems,
-                           (long long)ld, (const int *)ar->epoch, (const uint32_t *)ar->flags[ar->rank], ar->world, tns,
-                           status, residual, weight, out, cols, eps);
+    e = launch_ex(rmsnorm_ar_kernel<__half>, grid, block, 0, s, kArCluster, pdl, (const float *)ar->mc_f32,
+                  (long long)ar->slot_elems, (long long)ld, (const int *)ar->epoch,
+                  (const uint32_t *)ar->flags[ar->rank], ar->world, tns, status, residual, weight, out, cols, eps, pdl);
   else
-    e = cudaLaunchKernelEx(&cfg, rmsnorm_ar_kernel<__nv_bfloat16>, (const float *)ar->mc_f32,
-                           (long long)ar->slot_elems, (long long)ld, (const int *)ar->epoch,
-                           (const uint32_t *)ar->flags[ar->rank], ar->world, tns, status, residual, weight, out, cols,
-                           eps);
+    e = launch_ex(rmsnorm_ar_kernel<__nv_bfloat16>, grid, block, 0, s, kArCluster, pdl, (const float *)ar->mc_f32,
+                  (long long)ar->slot_elems, (long long)ld, (const int *)ar->epoch,
+                  (const uint32_t *)ar->flags[ar->rank], ar->world, tns, status, residual, weight, out, cols, eps, pdl);
   if (e != cudaSuccess) return cuda_status(e, "rmsnorm_allreduce launch");
   return cuda_status(cudaGetLastError(), "rmsnorm_allreduce launch");
 }

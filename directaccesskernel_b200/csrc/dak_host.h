@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "dak_linear.cuh"
 
 namespace dak {
@@ -28,6 +30,43 @@ int check_gpu_accessible(const void *p, const char *what);
 // budget, and the tcgen05 kernel only follows it while two CTAs' TMEM columns
 // fit in one SM.
 uint32_t linear_smem_budget();
+
+// Programmatic dependent launch of the decode-step kernels (RMSNorm, rotary,
+// SiLU-gate, KV append, decode attention and its merge): off unless
+// DAK_B200_PDL_DECODE=1, and never with DAK_B200_NO_PDL=1.  When on, each of
+// them is launched with programmatic stream serialization, waits for the
+// previous kernel (griddepcontrol.wait) before it touches memory, and lets the
+// next kernel be scheduled, so launches overlap the tail of the kernel before.
+bool decode_pdl_enabled();
+
+// cudaLaunchKernelEx with optional 1-D clusters (cluster > 1) and programmatic
+// stream serialization (pdl).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster,
+                      bool pdl, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Shared-memory bytes and launch of the CUDA-core kernel for `ntok_tmpl`
 // (1, 2, 4 or 8) tokens and dtype (DAK_DTYPE_F16 / _BF16).  With grid == 0

@@ -29,12 +29,14 @@ struct KvAppendParams {
   int max_pages;                       // table entries per sequence
   int kv_heads, row_bytes, page_size;
   int *status;
+  int pdl;                             // launched with programmatic stream serialization
 };
 
 // One warp per (sequence, KV head): lanes split the K row and the V row into
 // 16-byte pieces.  Out-of-range table entries or positions are recorded in the
 // status word and skipped, never written.
 __global__ void __launch_bounds__(32) kv_append_kernel(const __grid_constant__ KvAppendParams p) {
+  pdl_enter(p.pdl);
   const int b = blockIdx.x / p.kv_heads;
   const int h = blockIdx.x - b * p.kv_heads;
   const int pos = p.positions[b];
@@ -116,6 +118,8 @@ extern "C" int dak_kv_append_paged(const dak_kv_append_args *a, void *stream) {
   p.page_size = a->page_size;
   p.status = device_status_word();
   if (!p.status) return fail(DAK_ERR_CUDA, "no device status word");
-  kv_append_kernel<<<a->batch * a->kv_heads, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return cuda_status(cudaGetLastError(), "KV append launch");
+  p.pdl = decode_pdl_enabled() ? 1 : 0;
+  const cudaError_t e = launch_ex(kv_append_kernel, dim3(a->batch * a->kv_heads), dim3(32), 0,
+                                  static_cast<cudaStream_t>(stream), 1, p.pdl != 0, p);
+  return cuda_status(e, "KV append launch");
 }

@@ -314,6 +314,16 @@ uint32_t linear_smem_budget() {
   return bytes;
 }
 
+bool decode_pdl_enabled() {
+  static const bool on = [] {
+    const char *off = getenv("DAK_B200_NO_PDL");
+    if (off && off[0] && off[0] != '0') return false;
+    const char *v = getenv("DAK_B200_PDL_DECODE");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
+}
+
 // ---------------------------------------------------------- the split linear
 namespace {
 constexpr int kAutoHostCtas = 8;  // two CTAs with 4 x 32 KB in flight already saturate PCIe Gen5
