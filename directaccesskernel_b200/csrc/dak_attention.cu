@@ -9,13 +9,15 @@
 // Here:
 //   * one CTA per (batch, KV head, split) serves all G = Hq/Hkv query heads of
 //     the GQA group, so every KV byte crosses the host link or HBM once;
-//   * K/V arrive as 64-token chunks through a 4-stage ring filled by TMA 4-D
+//   * K/V arrive as 64-token chunks through a 4-stage ring (3 stages and two
+//     CTAs per SM with DAK_B200_ATTN_STAGES=3) filled by TMA 4-D
 //     tile loads (128-byte swizzle) issued by one producer warp; each chunk is
 //     made of pages (64 tokens of one row in the reference's [B, H, S, D]
 //     layout, or page_size-token pages of a paged pool), and each page picks
 //     the host or the device tile map, so one sequence may span both tiers;
-//   * 4 compute warps do FP32 q.k, an online softmax (expf) and p.V on CUDA
-//     cores (the kernel is bound by memory, not math);
+//   * 4 compute warps do q.k and p.V on the tensor cores (mma.sync m16n8k16,
+//     FP32 accumulators; the group's query heads are the M rows) with an
+//     online softmax (expf) per warp, merged across warps at the end;
 //   * per-split (o, m, l) go to caller-provided FP32 scratch and a second
 //     kernel merges the splits with log-sum-exp, as kernel.cuh:362-386 does.
 #include <cfloat>
@@ -29,7 +31,7 @@ namespace {
 
 constexpr int kHeadDim = 128;
 constexpr int kChunk = 64;          // tokens per pipeline stage
-constexpr int kAttnStages = 4;
+constexpr int kAttnStages = 4;      // default ring depth (one CTA per SM)
 constexpr int kAttnComputeWarps = 4;
 constexpr int kAttnThreads = (kAttnComputeWarps + 1) * 32;
 constexpr int kMaxGroup = 8;
@@ -58,17 +60,23 @@ struct alignas(64) AttnParams {
   int pdl;                 // launched with programmatic stream serialization
 };
 
+// Shared memory of a CTA with an ST-stage ring.  Below the default depth the
+// warps' partial outputs (ored, 4 x G x 128 FP32), merged after the last chunk
+// has been consumed, reuse the ring: with 3 stages a CTA needs about 98 KB and
+// two CTAs share an SM, so one CTA's start-up overlaps the other's stream.
+template <int ST>
 struct AttnSmem {
+  static constexpr bool ored_in_ring = ST < kAttnStages;
   static constexpr uint32_t kv_off = 0;
-  static constexpr uint32_t q_off = kv_off + kAttnStages * kStageBytes;      // G x 128 fp32
-  static constexpr uint32_t p_off = q_off + kMaxGroup * kHeadDim * 4;         // 64 x G fp32
-  static constexpr uint32_t redmax_off = p_off + kChunk * kMaxGroup * 4;      // 2 x 4 x G
-  static constexpr uint32_t ored_off = redmax_off + 2 * kAttnComputeWarps * kMaxGroup * 4;  // 4 x G x 128
-  static constexpr uint32_t lred_off = ored_off + kAttnComputeWarps * kMaxGroup * kHeadDim * 4;
-  static constexpr uint32_t tab_off = lred_off + kAttnComputeWarps * kMaxGroup * 4;  // block-table window
+  static constexpr uint32_t ored_off = ored_in_ring ? kv_off : kv_off + ST * kStageBytes;  // 4 x G x 128
+  static constexpr uint32_t redmax_off =
+      ored_in_ring ? kv_off + ST * kStageBytes : ored_off + kAttnComputeWarps * kMaxGroup * kHeadDim * 4;  // 4 x G
+  static constexpr uint32_t lred_off = redmax_off + kAttnComputeWarps * kMaxGroup * 4;  // 4 x G
+  static constexpr uint32_t tab_off = lred_off + kAttnComputeWarps * kMaxGroup * 4;     // block-table window
   static constexpr uint32_t bar_off = tab_off + kTabWindow * 4;
-  static constexpr uint32_t flag_off = bar_off + 2 * kAttnStages * 8;
+  static constexpr uint32_t flag_off = bar_off + 2 * ST * 8;
   static constexpr uint32_t bytes = flag_off + 16 + 1024;
+  static_assert(kAttnComputeWarps * kMaxGroup * kHeadDim * 4 <= ST * kStageBytes, "ored must fit in the ring");
 };
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
@@ -132,13 +140,13 @@ __device__ __forceinline__ PageLoc locate(const AttnParams &p, int b, int tok0) 
   return l;
 }
 
-template <typename T, int G>
+template <typename T, int G, int ST>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
   const uint32_t sbase = smem_u32(smem);
-  using S = AttnSmem;
+  using S = AttnSmem<ST>;
   pdl_enter(p.pdl);  // q, the newest K/V and seq_lens come from the kernels before
 
   const int warp = warp_id();
@@ -155,12 +163,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
   float *ored = reinterpret_cast<float *>(smem + S::ored_off);
   float *lred = reinterpret_cast<float *>(smem + S::lred_off);
   const uint32_t full0 = sbase + S::bar_off;
-  const uint32_t empty0 = full0 + kAttnStages * 8;
+  const uint32_t empty0 = full0 + ST * 8;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::flag_off);
   const WaitCtx wc{abort_flag, p.status};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kAttnStages; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, kAttnComputeWarps);
     }
@@ -187,8 +195,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
       int win = -kTabWindow;                          // first page held in tab_s
       uint32_t issued_mask = 0, issued_par = 0;
       for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kAttnStages;
-        const uint32_t ph = (uint32_t)((c / kAttnStages) & 1);
+        const int s = c % ST;
+        const uint32_t ph = (uint32_t)((c / ST) & 1);
         const int c0 = t_begin + c * kChunk;
         const int valid = min(kChunk, t_end - c0);
         const int npages = (valid + psz - 1) / psz;
@@ -233,7 +241,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
       if (lane == 0 && *abort_flag) {
         const WaitCtx drain{reinterpret_cast<volatile int *>(smem + S::flag_off + 4), p.status};
         *drain.abort = 0;
-        for (int st = 0; st < kAttnStages; ++st)
+        for (int st = 0; st < ST; ++st)
           if (issued_mask & (1u << st)) mbar_wait<false>(full0 + 8 * st, (issued_par >> st) & 1u, drain);
       }
     }
@@ -275,8 +283,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
     for (int j = 0; j < 4; ++j) o[nt][j] = 0.f;
 
   for (int c = 0; c < nchunks; ++c) {
-    const int s = c % kAttnStages;
-    const uint32_t ph = (uint32_t)((c / kAttnStages) & 1);
+    const int s = c % ST;
+    const uint32_t ph = (uint32_t)((c / ST) & 1);
     const bool ok = mbar_wait<false>(full0 + 8 * s, ph, wc);
     const uint32_t kst = sbase + S::kv_off + s * kStageBytes;
     const uint32_t vst = kst + kKvChunkBytes;
@@ -374,6 +382,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
   l += __shfl_xor_sync(0xffffffffu, l, 2);
   float *mred = redmax;                                  // [warp][G]
   float *lr = lred;                                      // [warp][G]
+  // When ored reuses the ring, every warp must be done reading its last chunk.
+  if constexpr (S::ored_in_ring) named_sync(1, kAttnComputeWarps * 32);
   if (r < G) {
     if (cq == 0) {
       mred[warp * kMaxGroup + r] = m_run;
@@ -436,24 +446,37 @@ __global__ void __launch_bounds__(kHeadDim) attn_merge_kernel(const __grid_const
   out[d] = Elem<T>::from_float(den == 0.f ? 0.f : acc / den);
 }
 
-template <typename T, int G>
+// Ring depth of the decode-attention kernel: 4 stages (one CTA per SM) by
+// default; DAK_B200_ATTN_STAGES=3 selects the 3-stage ring, with which two
+// CTAs share an SM.
+int attn_stages() {
+  static const int st = [] {
+    const char *v = getenv("DAK_B200_ATTN_STAGES");
+    return (v && v[0] == '3' && v[1] == 0) ? 3 : kAttnStages;
+  }();
+  return st;
+}
+
+template <typename T, int G, int ST>
 cudaError_t launch_g(const AttnParams &p, cudaStream_t stream) {
-  auto kern = attn_decode_kernel<T, G>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AttnSmem::bytes);
+  auto kern = attn_decode_kernel<T, G, ST>;
+  constexpr uint32_t smem = AttnSmem<ST>::bytes;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = p.batch * p.num_kv_heads * p.num_splits;
-  e = launch_ex(kern, dim3(grid), dim3(kAttnThreads), AttnSmem::bytes, stream, 1, p.pdl != 0, p);
+  e = launch_ex(kern, dim3(grid), dim3(kAttnThreads), smem, stream, 1, p.pdl != 0, p);
   if (e != cudaSuccess || p.num_splits == 1) return e;
   return launch_ex(attn_merge_kernel<T>, dim3(p.batch * p.num_q_heads), dim3(kHeadDim), 0, stream, 1, p.pdl != 0, p);
 }
 
 template <typename T>
 cudaError_t launch_t(const AttnParams &p, int group, cudaStream_t stream) {
+  const bool three = attn_stages() == 3;
   switch (group) {
-    case 1: return launch_g<T, 1>(p, stream);
-    case 2: return launch_g<T, 2>(p, stream);
-    case 4: return launch_g<T, 4>(p, stream);
-    case 8: return launch_g<T, 8>(p, stream);
+    case 1: return three ? launch_g<T, 1, 3>(p, stream) : launch_g<T, 1, kAttnStages>(p, stream);
+    case 2: return three ? launch_g<T, 2, 3>(p, stream) : launch_g<T, 2, kAttnStages>(p, stream);
+    case 4: return three ? launch_g<T, 4, 3>(p, stream) : launch_g<T, 4, kAttnStages>(p, stream);
+    case 8: return three ? launch_g<T, 8, 3>(p, stream) : launch_g<T, 8, kAttnStages>(p, stream);
     default: return cudaErrorInvalidValue;
   }
 }
