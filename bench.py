@@ -8,7 +8,9 @@ ratio r in {0, .25, .5, .75, 1}.  One step is one pass over the whole sweep
 reference-facing module API (LinearHorizontal for 0 < r < 1, Linear on "cuda"
 / "cpu" for r = 0 / 1, as placement.py places them).  Weights total 436 MB
 per (M, r) pass, larger than the 126 MB L2, so no flush is needed between
-steps.  ``--workload attention`` runs BASELINE config 3 instead.
+steps.  ``--workload attention`` runs BASELINE config 3 instead;
+``--workload prefill`` runs the same layers at 512 tokens (the large-N path),
+against a roofline that adds the tensor-core term 2 M N K / peak.
 
 Metric: effective weight GB/s (weight bytes / time, benchmark_linear.py:341),
 with a roofline of max((1-r) W / HBM, r W / host link) per layer.
@@ -37,6 +39,10 @@ LLAMA8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 4096), "do
 TOKENS = (1, 4, 16, 64)
 RATIOS = (0.0, 0.25, 0.5, 0.75, 1.0)
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS = 1590.0
+FALLBACK_TFLOPS_SUSTAINED = 1400.0
+# Tokens per launch of the tcgen05 linear kernel; larger batches run in chunks.
+MMA_MAX_TOKENS = 256
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch divided by
 # the launch's device-tier bytes ((1 - r) W + x + y), from full-size ncu captures
 # of the Llama-3-8B layers at r = 0 and 0.5 (profiles/linear_core_llama8b_m1.md,
@@ -54,7 +60,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["linear", "attention", "opt66b", "llama70b"], default="linear")
+    ap.add_argument("--workload", choices=["linear", "prefill", "attention", "opt66b", "llama70b"], default="linear",
+                    help="prefill: the Llama-3-8B layers at 512 tokens, r in {0, 0.5, 1} (large-N path)")
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
     ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
     ap.add_argument("--ctx", type=int, default=16384, help="llama70b: context tokens per sequence")
@@ -80,6 +87,17 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_tflops(sustained: bool = False) -> tuple[float, str]:
+    """Dense bf16/fp16 tensor throughput (cuBLAS GEMM) from MEASURED_PEAKS.json."""
+    p = REPO / "MEASURED_PEAKS.json"
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if key in d:
+            return float(d[key]), "measured"
+    return (FALLBACK_TFLOPS_SUSTAINED if sustained else FALLBACK_TFLOPS), "fallback"
 
 
 # ------------------------------------------------------------------- clocks
@@ -191,6 +209,20 @@ def hbm_read_probe(torch, runtime):
 
 
 # ---------------------------------------------------------------- workload
+def layer_roofline(m: int, n: int, k: int, host_bytes: int, hbm_gbs: float, host_gbs: float,
+                   tflops: float, dtype_bytes: int = 2) -> tuple[str, float]:
+    """Lower bound (seconds) of one y[m, n] = x[m, k] W^T call whose weight has
+    ``host_bytes`` on the host: the slowest of the HBM stream (device weight rows
+    plus x and y), the host-link stream and the tensor-core work."""
+    w_bytes = n * k * dtype_bytes
+    io = (m * k + m * n) * dtype_bytes
+    terms = {"hbm": (w_bytes - host_bytes + io) / (hbm_gbs * 1e9),
+             "host": host_bytes / (host_gbs * 1e9),
+             "tensor": 2.0 * m * n * k / (tflops * 1e12)}
+    which = max(terms, key=terms.get)
+    return which, terms[which]
+
+
 def build_layers(torch, tokens, ratios, seed=0):
     """One module per (shape, ratio), placed as placement.py places it."""
     from directaccesskernel_b200.layers import Linear, LinearHorizontal
@@ -226,9 +258,12 @@ def build_layers(torch, tokens, ratios, seed=0):
 def run_linear(args, torch, rank, world):
     from directaccesskernel_b200 import runtime
 
-    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else list(TOKENS)
-    ratios = [float(r) for r in args.ratios.split(",")] if args.ratios else list(RATIOS)
+    prefill = args.workload == "prefill"
+    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else ([512] if prefill else list(TOKENS))
+    ratios = ([float(r) for r in args.ratios.split(",")] if args.ratios
+              else ([0.0, 0.5, 1.0] if prefill else list(RATIOS)))
     hbm_gbs, peak_kind = measured_peaks()
+    tflops, tflops_kind = measured_tensor_tflops()
     dma_gbs, tma_host_gbs = host_link_probe(torch, runtime, world)
     host_gbs = max(dma_gbs, tma_host_gbs)
     hbm_read_gbs = hbm_read_probe(torch, runtime)
@@ -352,16 +387,20 @@ def run_linear(args, torch, rank, world):
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
     total_ms, kernel_ms, e2e_ms = times.tolist()
 
-    # Roofline per launch: max((1-r) W / HBM, r W / host); x and y bytes ride with HBM.
+    # Roofline per layer call: max((1-r) W / HBM, r W / host, 2 M N K / tensor peak);
+    # x and y bytes ride with HBM.  The compute term only binds for prefill-sized
+    # M (at M = 64 it is a quarter of the HBM term).
     roof_ms = 0.0
     alg_bytes = 0
     dram_bytes = 0.0
     per_ratio = {}
+    bound_ms = {"hbm": 0.0, "host": 0.0, "tensor": 0.0}
     for i, (l, m) in enumerate(calls):
         io = (m * l["k"] + m * l["n"]) * 2
         dram_bytes += (l["w_bytes"] - l["host_bytes"] + io) * DRAM_PER_DEVICE_BYTE
-        t_roof = max((l["w_bytes"] - l["host_bytes"] + io) / (hbm_gbs * 1e9),
-                     l["host_bytes"] / (host_gbs * 1e9)) * 1e3
+        which, t_roof_s = layer_roofline(m, l["n"], l["k"], l["host_bytes"], hbm_gbs, host_gbs, tflops)
+        t_roof = t_roof_s * 1e3
+        bound_ms[which] += t_roof * args.steps
         roof_ms += t_roof * args.steps
         alg_bytes += l["w_bytes"] + io
         pr = per_ratio.setdefault(l["ratio"], {"bytes": 0, "ms": ratio_ms[l["ratio"]], "roof_ms": 0.0,
@@ -385,26 +424,37 @@ def run_linear(args, torch, rank, world):
                for i, (l, m) in enumerate(calls)]
     if args.details and rank == 0:
         Path(args.details).write_text(json.dumps(details, indent=1))
+    if prefill:
+        metric = f"offloaded linear effective weight GB/s (Llama-3-8B layers, prefill M={tokens})"
+        workload = (f"large-N prefill: Llama-3-8B qkv/o/gate_up/down x M{tokens} x r{ratios}; the tcgen05 kernel "
+                    f"takes {MMA_MAX_TOKENS} tokens per launch")
+    else:
+        metric = "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)"
+        workload = "BASELINE config 2: Llama-3-8B qkv/o/gate_up/down x M{1,4,16,64} x r{0,.25,.5,.75,1}"
     line = {
-        "metric": "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)",
+        "metric": metric,
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic N(0,0.02) weights, N(0,1) activations",
-        "config": {"workload": "BASELINE config 2: Llama-3-8B qkv/o/gate_up/down x M{1,4,16,64} x r{0,.25,.5,.75,1}",
+        "config": {"workload": workload,
                    "tokens": tokens, "ratios": ratios, "layers_per_step": len(calls),
                    "weight_bytes_per_step": w_bytes_step, "host_rows": "first (reference split_horizontal)",
                    "l2": "no flush: 436 MB of weights per (M, r) pass exceed the 126 MB L2",
                    "timing": "device: one CUDA graph per step (80 launches) replayed K times; "
                              "per-launch breakdown: per-layer graphs back to back with events between",
                    "parallelism": f"replicas x{world} (weak, no collective)"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": round(peak_eff, 2), "unit": "GB/s",
+        "roofline": {"bound": "tensor" if bound_ms["tensor"] > bound_ms["hbm"] + bound_ms["host"] else "hbm",
+                     "achieved": round(achieved, 2), "peak": round(peak_eff, 2), "unit": "GB/s",
                      "frac": round(achieved / peak_eff, 4),
                      "traffic": round(dram_bytes / len(calls)),
                      "traffic_basis": "DRAM bytes per launch, step average: ncu dram read+write = "
                                       f"{DRAM_PER_DEVICE_BYTE} x device-tier bytes on full-size captures; the "
                                       "host tier's bytes cross PCIe, so traffic < algorithmic bytes "
                                       f"({round(alg_bytes / len(calls))} per launch)",
-                     "peak_model": "combined HBM + host-link roofline, sum over layers of max((1-r)W/HBM, rW/host)",
+                     "peak_model": "combined HBM + host-link (+ tensor) roofline, sum over layers of "
+                                   "max((1-r)W/HBM, rW/host, 2MNK/tensor peak)",
+                     "bound_ms_by_term": {k: round(v, 4) for k, v in bound_ms.items()},
+                     "tensor_tflops": tflops, "tensor_peak_kind": tflops_kind,
                      "hbm_gbs": hbm_gbs, "hbm_peak_kind": peak_kind, "host_link_gbs": round(host_gbs, 2),
                      "host_link_dma_gbs": round(dma_gbs, 2), "host_link_tma_probe_gbs": round(tma_host_gbs, 2),
                      "hbm_read_probe_gbs": round(hbm_read_gbs, 1),
@@ -415,7 +465,7 @@ def run_linear(args, torch, rank, world):
                      "timing": "achieved = algorithmic bytes / device time of the step graph; per_ratio from one "
                                "graph per ratio; isolated_launch_frac from single-launch graphs with events between"},
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": len(calls) * args.steps,
+        "gpu_launches": sum(-(-m // MMA_MAX_TOKENS) for (l, m) in calls) * args.steps,
         "clocks": clock,
     }
     if cpu is not None:
@@ -925,7 +975,8 @@ def run_reference(args):
             "cpu_baseline": cpu,
             "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
-    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else list(TOKENS)
+    prefill = args.workload == "prefill"
+    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else ([512] if prefill else list(TOKENS))
     for _ in range(max(0, min(args.warmup, 1))):
         cpu_baseline_linear(tokens[:1], budget_s=5.0)
     vals = []
@@ -937,11 +988,13 @@ def run_reference(args):
     cpu = cpu_baseline_linear(tokens[:1], budget_s=2.0)
     cpu["value"] = v
     return {
-        "metric": "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)", "impl": "reference",
+        "metric": (f"offloaded linear effective weight GB/s (Llama-3-8B layers, prefill M={tokens})" if prefill
+                   else "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)"), "impl": "reference",
         "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(elapsed / max(1, args.steps) * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "BASELINE config 2 sample on host cores", "tokens": tokens},
+        "config": {"workload": ("large-N prefill" if prefill else "BASELINE config 2") + " sample on host cores",
+                   "tokens": tokens},
         "cpu_baseline": {**cpu, "kind": "port"},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

@@ -40,3 +40,20 @@ def test_auto_split_size_fills_whole_waves(batch, heads, seq):
     cost = lambda s, n: math.ceil(batch * heads * n / 148) * (s // 64 + 2)  # noqa: E731
     assert cost(sp, splits) <= cost(old, old_splits)
     assert ctas >= 1
+
+
+def test_layer_roofline_terms():
+    """The per-layer bound bench.py reports: HBM for the decode sweep (the tensor
+    term is at most a quarter of it at M = 64), tensor cores for HBM-resident
+    weights at prefill size, and the host link once half the rows are offloaded."""
+    hbm, host, tf = 6452.5, 51.3, 1642.4
+    for n, k in bench.LLAMA8B.values():
+        for m in bench.TOKENS:
+            which, t = bench.layer_roofline(m, n, k, 0, hbm, host, tf)
+            assert which == "hbm"
+            assert 2.0 * m * n * k / (tf * 1e12) <= 0.26 * t
+        which, t = bench.layer_roofline(512, n, k, 0, hbm, host, tf)
+        assert which == "tensor" and t == pytest.approx(2.0 * 512 * n * k / (tf * 1e12))
+        half = n * k  # bytes: half of the 2 n k weight bytes
+        which, t = bench.layer_roofline(512, n, k, half, hbm, host, tf)
+        assert which == "host" and t == pytest.approx(half / (host * 1e9))
