@@ -85,6 +85,17 @@ cudaError_t launch_linear_mma(const LinearParams &p, int ntok_tmpl, int dtype, i
                               int cluster, size_t smem, cudaStream_t stream,
                               int *max_clusters = nullptr);
 
+// The wide tcgen05 kernel: 257..512 tokens per launch, each weight tile
+// streamed once for both 256-token halves; no split-K, no clusters.  Its
+// weight tile maps use boxes of 64 features x linear_wide_k_rows() K rows and
+// its activation map boxes of 64 K x 256 tokens.
+size_t linear_wide_smem_bytes();
+int linear_wide_k_rows();
+cudaError_t launch_linear_wide(const LinearParams &p, int dtype, int grid, size_t smem, cudaStream_t stream);
+// Off unless DAK_B200_WIDE_PREFILL=1: batches above 256 tokens of a layer with
+// host-resident rows then go to the wide kernel in chunks of up to 512 tokens.
+bool wide_prefill_enabled();
+
 // Sets, once per kernel and device, the kernel's dynamic shared-memory limit
 // to the device's opt-in maximum and allows non-portable cluster sizes.  Every
 // launch of the kernel, of any size, then fits the function's attributes, also

@@ -324,6 +324,14 @@ bool decode_pdl_enabled() {
   return on;
 }
 
+bool wide_prefill_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("DAK_B200_WIDE_PREFILL");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
+}
+
 // ---------------------------------------------------------- the split linear
 namespace {
 constexpr int kAutoHostCtas = 8;  // two CTAs with 4 x 32 KB in flight already saturate PCIe Gen5
@@ -420,6 +428,57 @@ int check_ptr16(const void *p, const char *what) {
   return DAK_OK;
 }
 
+// One chunk of 257..512 tokens on the wide kernel.  Every CTA walks an even
+// share of whole 64-feature boxes of its tier.  The host tier gets up to
+// kWideHostCtas CTAs: each keeps two 16 KB weight stages in flight, so 32 of
+// them hold about 1 MB in flight, several times what the host link needs.  The
+// device tier, bound by tensor-core work at this batch size, gets the rest of
+// the SMs (one CTA per SM: the kernel takes about 161 KB of shared memory).
+constexpr int kWideHostCtas = 32;
+
+int run_linear_wide_chunk(const dak_linear_args *a, const DeviceInfo *dev, int64_t t0, int64_t nt,
+                          cudaStream_t stream) {
+  const int boxes_h = (int)((a->host_cols + kBoxCols - 1) / kBoxCols);
+  const int boxes_d = (int)((a->dev_cols + kBoxCols - 1) / kBoxCols);
+  const int hc = boxes_h > 0 ? std::max(1, std::min({kWideHostCtas, boxes_h, dev->num_sms / 2})) : 0;
+  const int dc = boxes_d > 0 ? std::max(1, std::min(dev->num_sms - hc, boxes_d)) : 0;
+  const int64_t tiers_cols[2] = {a->host_cols, a->dev_cols};
+  const void *tiers_w[2] = {a->w_host, a->w_dev};
+  const int64_t tiers_ld[2] = {a->ld_host, a->ld_dev};
+  const int64_t tiers_off[2] = {a->host_col_offset, a->dev_col_offset};
+  const int ctas[2] = {hc, dc};
+  LinearParams p;
+  std::memset(&p, 0, sizeof(p));
+  int st;
+  for (int t = 0; t < 2; ++t) {
+    LinearTier &tr = p.tier[t];
+    tr.cols = (int)tiers_cols[t];
+    tr.col_offset = (int)tiers_off[t];
+    tr.cta_begin = t == 0 ? 0 : hc;
+    tr.cta_count = ctas[t];
+    tr.ksplit = 1;
+    if (tr.cols > 0 && tr.cta_count > 0 &&
+        (st = tile_map_2d(&tr.wmap, tiers_w[t], a->dtype, a->K, tiers_cols[t], tiers_ld[t], kBoxCols,
+                          linear_wide_k_rows(), 128)))
+      return st;
+  }
+  const void *x = static_cast<const uint16_t *>(a->x) + t0 * a->ldx;
+  if ((st = tile_map_2d(&p.xmap, x, a->dtype, nt, a->K, a->ldx, kBoxCols, kMmaMaxTok, 128))) return st;
+  p.y = static_cast<uint16_t *>(a->y) + t0 * a->ldy;
+  p.ldy = a->ldy;
+  p.ntok = (int)nt;
+  p.K = (int)a->K;
+  p.status = dev->status;
+  p.pdl = pdl_enabled() ? 1 : 0;
+  const size_t smem = linear_wide_smem_bytes();
+  if ((int)smem > dev->max_smem_optin) return fail(DAK_ERR_UNSUPPORTED, "wide linear: shared memory plan too large");
+  if (trace_plans())
+    fprintf(stderr, "[dak plan] wide ntok=%lld K=%lld host_cols=%lld dev_cols=%lld | host ctas=%d | dev ctas=%d\n",
+            (long long)nt, (long long)a->K, (long long)a->host_cols, (long long)a->dev_cols, hc, dc);
+  const cudaError_t e = launch_linear_wide(p, a->dtype, hc + dc, smem, stream);
+  return e == cudaSuccess ? DAK_OK : cuda_status(e, "wide linear kernel launch");
+}
+
 int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar = nullptr) {
   if (!a) return fail(DAK_ERR_INVALID_ARG, "args is null");
   if (a->dtype != DAK_DTYPE_F16 && a->dtype != DAK_DTYPE_BF16)
@@ -469,10 +528,16 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
   const int max_ks = mma ? kMmaMaxKsplitHost : kCoreMaxKsplit;
   const int nkb = (int)((a->K + bk - 1) / bk);
 
-  // Token chunks: the tcgen05 kernel serves up to 256 tokens per launch.
-  const int64_t chunk = mma ? kMmaMaxTok : kCoreMaxTok;
+  // Token chunks: the tcgen05 kernel serves up to 256 tokens per launch; the
+  // wide kernel, when enabled, up to 512 for a layer with host-resident rows.
+  const bool wide = mma && !ar && a->host_cols > 0 && a->ntok > kMmaMaxTok && wide_prefill_enabled();
+  const int64_t chunk = wide ? 2 * kMmaMaxTok : mma ? kMmaMaxTok : kCoreMaxTok;
   for (int64_t t0 = 0; t0 < a->ntok; t0 += chunk) {
     const int64_t nt = std::min(chunk, a->ntok - t0);
+    if (wide && nt > kMmaMaxTok) {
+      if ((st = run_linear_wide_chunk(a, dev, t0, nt, stream))) return st;
+      continue;
+    }
     int tmpl = 1;
     if (mma) {
       tmpl = 16;

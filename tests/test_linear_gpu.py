@@ -5,6 +5,8 @@ Tolerance (from the task's parity bar): normwise max relative error
 max|y - y_ref| / max|y_ref| <= 1e-2 against FP32/FP64 accumulation; the
 kernels accumulate in FP32 and round once to 16 bits, so the observed error is
 about 1e-3."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -68,6 +70,25 @@ def test_tcgen05_path(shape, ntok):
     w, x = _inputs(*shape, ntok, seed=1)
     ref = _oracle(w, x)
     for host_cols in (0, 128, shape[0]):
+        y = _split_run(w, x, host_cols, path=_lib.PATH_TCGEN05)
+        assert not np.isnan(y).any()
+        assert rel_err(y, ref) < TOL, (host_cols, rel_err(y, ref))
+
+
+@pytest.mark.skipif(os.environ.get("DAK_B200_WIDE_PREFILL") != "1",
+                    reason="the wide prefill kernel is opt-in: run with DAK_B200_WIDE_PREFILL=1")
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("ntok", [257, 300, 512, 700, 1024])
+@pytest.mark.parametrize("shape", [(256, 512), (384, 200), (1088, 4160)])
+def test_wide_prefill_path(shape, ntok, dtype):
+    """Batches of 257..512 tokens per chunk on a layer with host rows go to the
+    wide kernel (each weight tile once for both 256-token halves); ragged
+    batches, a K that is not a multiple of 64 and partial 64-feature boxes."""
+    from directaccesskernel_b200 import _lib
+
+    w, x = _inputs(*shape, ntok, dtype=dtype, seed=7)
+    ref = _oracle(w, x)
+    for host_cols in (64, 128, shape[0]):
         y = _split_run(w, x, host_cols, path=_lib.PATH_TCGEN05)
         assert not np.isnan(y).any()
         assert rel_err(y, ref) < TOL, (host_cols, rel_err(y, ref))
