@@ -74,6 +74,13 @@ class LlamaShape:
         return dtype_bytes * 2 * self.layers * batch * pages * PAGE * (self.kv_heads // world) * self.head_dim
 
 
+def vocab_rows_per_rank(vocab: int, world: int) -> int:
+    """lm_head rows each rank holds: the vocabulary split G ways, rounded up to
+    whole 64-row tiles.  Rows past the vocabulary are zero and never take part in
+    the greedy pick."""
+    return -(-vocab // (world * 64)) * 64
+
+
 def budget_fraction(shape: LlamaShape, world: int, batch: int, ctx: int, hbm_budget_bytes: int) -> float:
     """Host fraction f of both weights and KV such that (1 - f) x (this rank's weights
     + KV) fits the per-GPU HBM budget (0 when everything fits)."""
@@ -111,9 +118,7 @@ class TPLlamaDecoder(nn.Module):
         if shape.head_dim != 128:
             raise ValueError("the decode attention kernel serves head_dim 128")
         self.hq, self.hkv, self.ffn_r = shape.heads // G, shape.kv_heads // G, shape.ffn // G
-        # Vocabulary rows per rank, a whole number of 64-row tiles; rows past the
-        # vocabulary are zero and never take part in the greedy pick.
-        self.vocab_r = -(-shape.vocab // (G * 64)) * 64
+        self.vocab_r = vocab_rows_per_rank(shape.vocab, G)
         self.B, self.max_ctx, self.dtype, self.device = batch, max_ctx, dtype, device
         self.weight_offload = float(weight_offload)
         self.kv_host_fraction = float(kv_host_fraction)

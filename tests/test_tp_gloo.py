@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding and collectives with world_size 2 on CPU (gloo).
+"""Tensor-parallel sharding and collectives with world_size 2, 4 and 8 on CPU (gloo).
 
 The per-rank compute is a plain nn.Linear on the rank's shard, so these tests
 pin the sharding arithmetic and the collective wiring of
@@ -34,40 +34,41 @@ def _worker(rank, world, port, q):
 
 @torch.no_grad()
 def _run(rank, world, q):
-    if True:
-        from directaccesskernel_b200.tp import ColumnParallelLinear, RowParallelLinear, shard_cols, shard_rows
+    from directaccesskernel_b200.tp import ColumnParallelLinear, RowParallelLinear, shard_cols, shard_rows
 
-        torch.manual_seed(0)
-        w = torch.randn(96, 64, dtype=torch.float64)
-        x = torch.randn(3, 64, dtype=torch.float64)
-        ref = x @ w.T
+    torch.manual_seed(0)
+    w = torch.randn(96, 64, dtype=torch.float64)
+    x = torch.randn(3, 64, dtype=torch.float64)
+    ref = x @ w.T
+    step = 96 // world
 
-        def local(shard):
-            lin = torch.nn.Linear(shard.shape[1], shard.shape[0], bias=False, dtype=torch.float64)
-            with torch.no_grad():
-                lin.weight.copy_(shard)
-            return lin
+    def local(shard):
+        lin = torch.nn.Linear(shard.shape[1], shard.shape[0], bias=False, dtype=torch.float64)
+        with torch.no_grad():
+            lin.weight.copy_(shard)
+        return lin
 
-        col = ColumnParallelLinear(local(shard_rows(w, rank, world)), 96)
-        y_col = col(x)
-        col_sharded = ColumnParallelLinear(local(shard_rows(w, rank, world)), 96, gather_output=False)(x)
-        row = RowParallelLinear(local(shard_cols(w, rank, world)), 64)
-        y_row = row(x)
-        # An MLP-style pair: column-parallel (sharded output) feeding row-parallel.
-        w2 = torch.randn(64, 96, dtype=torch.float64)
-        up = ColumnParallelLinear(local(shard_rows(w, rank, world)), 96, gather_output=False)
-        down = RowParallelLinear(local(shard_cols(w2, rank, world)), 96, input_is_parallel=True)
-        y_mlp = down(up(x))
-        q.put((rank, float((y_col - ref).abs().max()), float((y_row - ref).abs().max()),
-               float((col_sharded - ref[:, rank * 48:(rank + 1) * 48]).abs().max()),
-               float((y_mlp - (x @ w.T) @ w2.T).abs().max())))
+    col = ColumnParallelLinear(local(shard_rows(w, rank, world)), 96)
+    y_col = col(x)
+    col_sharded = ColumnParallelLinear(local(shard_rows(w, rank, world)), 96, gather_output=False)(x)
+    row = RowParallelLinear(local(shard_cols(w, rank, world)), 64)
+    y_row = row(x)
+    # An MLP-style pair: column-parallel (sharded output) feeding row-parallel.
+    w2 = torch.randn(64, 96, dtype=torch.float64)
+    up = ColumnParallelLinear(local(shard_rows(w, rank, world)), 96, gather_output=False)
+    down = RowParallelLinear(local(shard_cols(w2, rank, world)), 96, input_is_parallel=True)
+    y_mlp = down(up(x))
+    q.put((rank, float((y_col - ref).abs().max()), float((y_row - ref).abs().max()),
+           float((col_sharded - ref[:, rank * step:(rank + 1) * step]).abs().max()),
+           float((y_mlp - (x @ w.T) @ w2.T).abs().max())))
 
 
-def test_tp_column_and_row_parallel_match_unsharded():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_column_and_row_parallel_match_unsharded(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
