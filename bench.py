@@ -823,7 +823,7 @@ def run_llama70b(args, torch, rank, world):
         roof_ms, host_gbs = mx[0].item(), -mx[1].item()
         host_step, dev_step = sm[0].item() / world, sm[1].item() / world
     step_ms = ms / K
-    launches_per_step = shape.layers * 6 + 1  # 4 linears, KV append, attention (+ merge) per layer; lm_head
+    launches_per_step = dec.kernel_launches_per_step()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_llama70b(B, ctx, shape.layers)

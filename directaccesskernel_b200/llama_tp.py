@@ -363,6 +363,15 @@ class TPLlamaDecoder(nn.Module):
                 self.logits_full = logits
         return self.next_ids
 
+    def kernel_launches_per_step(self) -> int:
+        """Launches of this library's kernels in one ``forward_step``: the first
+        RMSNorm; per layer the four linears, rotary, KV append, attention (plus the
+        split merge when a sequence spans several splits), SiLU-gate and two
+        RMSNorms; then lm_head.  The torch ops around them (embedding gather,
+        greedy pick) and NCCL's kernels are not counted."""
+        merge = 1 if -(-self.max_ctx // self.split) > 1 else 0
+        return 1 + len(self.layers) * (10 + merge) + 1
+
     def advance(self) -> None:
         """Feeds the greedy tokens back and moves every sequence one position on."""
         self.ids.copy_(self.next_ids)

@@ -100,3 +100,13 @@ def test_vocab_shards_tile_the_vocabulary(world, vocab):
         covered.extend(int(v) for v in rows)
         assert torch.all(dec.lm_head[dec.vocab_valid:] == 0)
     assert covered == list(range(vocab))
+
+
+def test_kernel_launch_count_per_step():
+    s = LlamaShape.from_config(decode.llama_config("llama-3-70b"))
+    dec = _cpu_rank(s, 0, 8)
+    dec.layers = list(range(20))
+    dec.max_ctx, dec.split = 16384 + 64, 1024
+    assert dec.kernel_launches_per_step() == 1 + 20 * 11 + 1
+    dec.split = dec.max_ctx  # one split: no merge kernel
+    assert dec.kernel_launches_per_step() == 1 + 20 * 10 + 1
