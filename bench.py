@@ -65,6 +65,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
     ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
     ap.add_argument("--ctx", type=int, default=16384, help="llama70b: context tokens per sequence")
+    ap.add_argument("--rank-of-tp", type=int, default=1,
+                    help="llama70b on 1 GPU: build one rank of a TP-N decoder (heads, KV heads, FFN and vocabulary "
+                         "divided by N) to profile its kernels on one GPU; there is no all-reduce")
     ap.add_argument("--nccl-allreduce", action="store_true",
                     help="llama70b: NCCL all-reduce after o and down instead of the fused path")
     ap.add_argument("--no-balance", action="store_true",
@@ -729,6 +732,9 @@ def run_llama70b(args, torch, rank, world):
     host_gbs = max(dma_gbs, tma_host_gbs)
     cfg = decode.llama_config("llama-3-70b", num_hidden_layers=args.layers)
     shape = LlamaShape.from_config(cfg)
+    emulated = args.rank_of_tp if world == 1 and args.rank_of_tp > 1 else 1
+    if emulated > 1:
+        shape = rank_shape(shape, emulated)
     B, ctx = args.batch, args.ctx
     W, K = max(3, args.warmup), args.steps
     max_ctx = ctx + W + K + 4
@@ -839,7 +845,8 @@ def run_llama70b(args, torch, rank, world):
                    "host_fraction": round(frac, 4), "per_rank_host_fractions": [round(f, 4) for f in fracs],
                    "rank0_host_bytes": int(lin_host + kv_host),
                    "rank0_device_bytes": int(lin_dev + kv_dev), "build_s": round(build_s, 1),
-                   "parallelism": f"tp{world}",
+                   "parallelism": f"tp{world}" if emulated == 1 else
+                                  f"one rank of tp{emulated} on 1 GPU (its kernels and shapes, no all-reduce)",
                    "allreduce": "fused: row-parallel kernels publish, the next RMSNorm reduces over NVSwitch "
                                 "multicast" if fused else "NCCL",
                    "l2": "tens of GB read per step exceed L2",
@@ -858,6 +865,20 @@ def run_llama70b(args, torch, rank, world):
         "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
         **({"cpu_baseline": cpu} if cpu is not None else {}),
     }
+
+
+def rank_shape(shape, tp: int):
+    """The per-rank layer shapes of a TP-``tp`` decoder as a one-rank model:
+    query heads, KV heads and FFN features divided by ``tp``, lm_head rows as one
+    rank's vocabulary shard.  The hidden size, head size and depth stay."""
+    import dataclasses
+
+    from directaccesskernel_b200.llama_tp import vocab_rows_per_rank
+
+    if shape.heads % tp or shape.kv_heads % tp or shape.ffn % tp:
+        raise ValueError(f"heads {shape.heads}, kv_heads {shape.kv_heads} and ffn {shape.ffn} must divide by {tp}")
+    return dataclasses.replace(shape, heads=shape.heads // tp, kv_heads=shape.kv_heads // tp, ffn=shape.ffn // tp,
+                               vocab=vocab_rows_per_rank(shape.vocab, tp))
 
 
 def balanced_host_fractions(mean_frac: float, bandwidths: list[float], lo: float = 0.0) -> list[float]:

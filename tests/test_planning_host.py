@@ -57,3 +57,20 @@ def test_layer_roofline_terms():
         half = n * k  # bytes: half of the 2 n k weight bytes
         which, t = bench.layer_roofline(512, n, k, half, hbm, host, tf)
         assert which == "host" and t == pytest.approx(half / (host * 1e9))
+
+
+def test_rank_shape_matches_a_tp8_rank():
+    """``bench.py --rank-of-tp 8`` builds one TP8 rank's layer shapes as a one-GPU
+    model: its per-rank weight bytes equal a TP8 rank's (up to the replicated
+    embedding, which holds one vocabulary shard instead of the full table)."""
+    from directaccesskernel_b200 import decode
+    from directaccesskernel_b200.llama_tp import LlamaShape
+
+    full = LlamaShape.from_config(decode.llama_config("llama-3-70b"))
+    r = bench.rank_shape(full, 8)
+    assert (r.heads, r.kv_heads, r.ffn, r.hidden, r.head_dim) == (8, 1, 3584, 8192, 128)
+    emb_full, emb_r = full.vocab * full.hidden * 2, r.vocab * r.hidden * 2
+    assert r.weight_bytes_per_rank(1) - emb_r + emb_full == pytest.approx(full.weight_bytes_per_rank(8), rel=1e-3)
+    assert r.kv_bytes_per_rank(1, 32, 16384) == full.kv_bytes_per_rank(8, 32, 16384)
+    with pytest.raises(ValueError):
+        bench.rank_shape(full, 3)
