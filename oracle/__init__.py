@@ -9,4 +9,5 @@ running the reference's own Python code (tests/test_oracle_golden.py).
 """
 from .attention import (batch_split_decode, decode_attention, decode_attention_grouped, lse_merge,  # noqa: F401
                         paged_decode, paged_gather, split_partials)
+from .kv_cache import paged_append, static_cache_update  # noqa: F401
 from .linear import gemv_horizontal, horizontal_split, linear, split_horizontal  # noqa: F401

@@ -48,6 +48,23 @@ def gen(seed: int, shape, dtype=np.float16, scale: float = 1.0) -> np.ndarray:
     return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(dtype)
 
 
+def kv_cache_updates():
+    """The update sequence of tests/golden/kv_cache.npz (make_golden.py, KV_UPDATES):
+    (positions, seed) per update: a 20-token prefill, ten single-token decode
+    steps, one scattered 3-token update; K from ``seed``, V from ``seed + 1000``."""
+    return [(list(range(20)), 500)] + [([t], 501 + t) for t in range(20, 30)] + [([35, 31, 33], 540)]
+
+
+# Positions the sequence above writes (the others keep their initial contents).
+KV_WRITTEN = sorted(set(range(30)) | {31, 33, 35})
+
+
+def kv_page_table(batch: int, pages: int) -> np.ndarray:
+    """Block table alternating device (v >= 0) and host (-1-v) pages, shifted per sequence."""
+    return np.array([[(b * pages + j) if (b + j) % 2 else -1 - (b * pages + j) for j in range(pages)]
+                     for b in range(batch)])
+
+
 def checksum(a: np.ndarray) -> str:
     import hashlib
 

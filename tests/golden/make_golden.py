@@ -21,6 +21,9 @@ Nothing here runs a reference GPU kernel.  What is pinned:
   attention_ref.npz      the attention hook's outputs (interface.py:142-189 ->
                          its transformers eager path) and vanila_llama's GQA
                          eager_attention_forward (vanila_llama.py:212-246)
+  kv_cache.npz           PinnedStaticCache (app/python/pinned_static_cache.py)
+                         after a prefill, single-token decode updates and a
+                         scattered multi-token update
 
 Inputs come from numpy's PCG64 generator with fixed seeds; the fixtures keep a
 checksum of every input so tests can tell if a numpy version draws differently.
@@ -340,22 +343,77 @@ def make_attention_ref(out: Path):
     np.savez_compressed(out / "attention_ref.npz", **res)
 
 
+# The host-KV cache update sequence: (cache_position or None, seed) per update,
+# applied to both layers (layer 1 always with explicit positions).
+KV_CACHE = {"layers": 2, "batch": 3, "hidden": 64, "heads": 4, "kv_heads": 2, "max_len": 48}
+KV_UPDATES = [(None, 500)] + [([t], 501 + t) for t in range(20, 30)] + [([35, 31, 33], 540)]
+KV_PREFILL = 20
+
+
+def kv_update_positions(i: int):
+    pos, _ = KV_UPDATES[i]
+    return list(range(KV_PREFILL)) if pos is None else pos
+
+
+def make_kv_cache(out: Path):
+    import torch
+    from app.python.pinned_static_cache import PinnedStaticCache
+
+    c = KV_CACHE
+    cfg = types.SimpleNamespace(num_hidden_layers=c["layers"], hidden_size=c["hidden"],
+                                num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"])
+    d = c["hidden"] // c["heads"]
+    with redirect_cuda("cpu"):
+        cache = PinnedStaticCache(cfg, c["batch"], c["max_len"], torch.float16)
+    shas = []
+    for i, (pos, seed) in enumerate(KV_UPDATES):
+        T = len(kv_update_positions(i))
+        k = gen(seed, (c["batch"], c["kv_heads"], T, d))
+        v = gen(seed + 1000, (c["batch"], c["kv_heads"], T, d))
+        shas.append(checksum(np.concatenate([k.ravel(), v.ravel()])))
+        for layer in range(c["layers"]):
+            kw = None
+            if pos is not None or layer == 1:
+                kw = {"cache_position": torch.tensor(kv_update_positions(i), dtype=torch.long)}
+            cache.update(torch.from_numpy(k), torch.from_numpy(v), layer, kw)
+    res = {"cfg": np.array([c[n] for n in ("layers", "batch", "hidden", "heads", "kv_heads", "max_len")]),
+           "seq_lengths": np.array([cache.get_seq_length(layer) for layer in range(c["layers"])]),
+           "input_sha": np.array(shas)}
+    for layer in range(c["layers"]):
+        res[f"k{layer}"] = cache.key_cache[layer].numpy()
+        res[f"v{layer}"] = cache.value_cache[layer].numpy()
+    np.savez_compressed(out / "kv_cache.npz", **res)
+
+
+MAKERS = ["split_tables", "desc_args", "linear_split", "placement", "linear_ref", "attention_ref", "kv_cache"]
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--ref", default="/root/reference", help="checkout of shouxulin/DirectAccessKernel")
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--only", nargs="*", choices=MAKERS, help="regenerate only these fixtures")
     args = ap.parse_args()
     ref = Path(args.ref)
     if not (ref / "app" / "python" / "utils.py").exists():
         raise SystemExit(f"{ref} is not a DirectAccessKernel checkout")
     out = Path(args.out)
     rt = install_reference(ref)
-    make_split_tables(out)
-    make_desc_args(out, rt)
-    make_linear_split(out)
-    make_placement(out)
-    make_linear_ref(out)
-    make_attention_ref(out)
+    want = set(args.only or MAKERS)
+    if "split_tables" in want:
+        make_split_tables(out)
+    if "desc_args" in want:
+        make_desc_args(out, rt)
+    if "linear_split" in want:
+        make_linear_split(out)
+    if "placement" in want:
+        make_placement(out)
+    if "linear_ref" in want:
+        make_linear_ref(out)
+    if "attention_ref" in want:
+        make_attention_ref(out)
+    if "kv_cache" in want:
+        make_kv_cache(out)
     for p in sorted(out.glob("*.json")) + sorted(out.glob("*.npz")):
         print(f"{p.name:24s} {p.stat().st_size:8d} B")
 

@@ -112,3 +112,40 @@ def test_append_argument_errors():
         kv_append_paged(kn.float(), kn.float(), kd, vd, kh, vh, table, pos)
     with pytest.raises(RuntimeError):
         kv_append_paged(kn, kn, kd, None, kh, vh, table, pos)
+
+
+def test_writer_matches_the_reference_pinned_static_cache():
+    """Fed the update sequence that tests/golden/kv_cache.npz ran through the
+    reference's PinnedStaticCache (app/python/pinned_static_cache.py:47-107), one
+    token per sequence and call, the paged writer holds exactly the reference
+    cache's tokens, in host and device pages, for both layers."""
+    from conftest import KV_WRITTEN, gen, golden_npz, kv_cache_updates, kv_page_table
+
+    from directaccesskernel_b200 import runtime
+    from directaccesskernel_b200.attention import kv_append_paged
+
+    d = golden_npz("kv_cache.npz")
+    layers, B, hidden, heads, hkv, S = (int(v) for v in d["cfg"])
+    D, P = hidden // heads, 8
+    npg = S // P
+    table = kv_page_table(B, npg)
+    tab = torch.from_numpy(table.astype(np.int32)).cuda()
+    pools = [_pools(B * npg, B * npg, hkv, P, D, seed=20 + layer) for layer in range(layers)]
+    for pos, seed in kv_cache_updates():
+        k = gen(seed, (B, hkv, len(pos), D))
+        v = gen(seed + 1000, (B, hkv, len(pos), D))
+        for layer in range(layers):
+            kd, vd, kh, vh = pools[layer]
+            for t, p in enumerate(pos):
+                kv_append_paged(torch.from_numpy(np.ascontiguousarray(k[:, :, t])).cuda(),
+                                torch.from_numpy(np.ascontiguousarray(v[:, :, t])).cuda(), kd, vd, kh, vh, tab,
+                                torch.full((B,), p, dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    assert runtime.device_status() == 0
+    for layer in range(layers):
+        kd, vd, kh, vh = (t.cpu().numpy() for t in pools[layer])
+        for b in range(B):
+            kb = oracle.paged_gather(kd, kh, table[b], S)
+            vb = oracle.paged_gather(vd, vh, table[b], S)
+            assert np.array_equal(kb[:, KV_WRITTEN], d[f"k{layer}"][b][:, KV_WRITTEN])
+            assert np.array_equal(vb[:, KV_WRITTEN], d[f"v{layer}"][b][:, KV_WRITTEN])

@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import checksum, gen, golden_json, golden_npz, rel_err
+from conftest import KV_WRITTEN, checksum, gen, golden_json, golden_npz, kv_cache_updates, kv_page_table, rel_err
 
 
 def test_split_horizontal_matches_reference():
@@ -106,3 +106,41 @@ def test_paged_gather_mixed_tiers():
             table.append(j // 2)
     got = oracle.paged_gather(dev, host, np.array(table), seq.shape[1])
     assert np.array_equal(got, seq)
+
+
+def test_static_cache_oracle_matches_pinned_static_cache():
+    """oracle.static_cache_update reproduces the reference's PinnedStaticCache
+    (app/python/pinned_static_cache.py:47-107) bit for bit, and the paged writer
+    restatement (one token per sequence and call, mixed host/device pages) holds
+    the same tokens."""
+    d = golden_npz("kv_cache.npz")
+    layers, B, hidden, heads, hkv, S = (int(v) for v in d["cfg"])
+    D = hidden // heads
+    caches = [[np.zeros((B, hkv, S, D), np.float16) for _ in range(2)] for _ in range(layers)]
+    P = 8
+    npg = S // P
+    table = kv_page_table(B, npg)
+    pools = [[np.zeros((B * npg, hkv, P, D), np.float16) for _ in range(4)] for _ in range(layers)]  # kd vd kh vh
+    seq = [0] * layers
+    for i, (pos, seed) in enumerate(kv_cache_updates()):
+        k = gen(seed, (B, hkv, len(pos), D))
+        v = gen(seed + 1000, (B, hkv, len(pos), D))
+        assert checksum(np.concatenate([k.ravel(), v.ravel()])) == str(d["input_sha"][i])
+        for layer in range(layers):
+            seq[layer] = max(seq[layer], oracle.static_cache_update(caches[layer][0], k, pos))
+            oracle.static_cache_update(caches[layer][1], v, pos)
+            kd, vd, kh, vh = pools[layer]
+            for t, p in enumerate(pos):
+                positions = np.full(B, p)
+                oracle.paged_append(kd, kh, table, positions, k[:, :, t])
+                oracle.paged_append(vd, vh, table, positions, v[:, :, t])
+    assert list(d["seq_lengths"]) == seq == [36, 36]
+    written = KV_WRITTEN
+    for layer in range(layers):
+        assert np.array_equal(caches[layer][0], d[f"k{layer}"]) and np.array_equal(caches[layer][1], d[f"v{layer}"])
+        kd, vd, kh, vh = pools[layer]
+        for b in range(B):
+            kb = oracle.paged_gather(kd, kh, table[b], S)
+            vb = oracle.paged_gather(vd, vh, table[b], S)
+            assert np.array_equal(kb[:, written], d[f"k{layer}"][b][:, written])
+            assert np.array_equal(vb[:, written], d[f"v{layer}"][b][:, written])
