@@ -48,6 +48,9 @@ struct WideLayout {
   static constexpr uint32_t misc_off = bar_off + (2 * kWideStages + 3) * 8;  // tmem slot, abort flags
   static constexpr uint32_t bytes = misc_off + 16 + 1024;                     // + alignment slack
 };
+static_assert(WideLayout::bytes <= 227 * 1024, "two wide stages must fit one CTA's shared memory");
+static_assert(WideLayout::x_off % 1024 == 0 && kWideXBox % 1024 == 0 && kWideWBox % 1024 == 0,
+              "128-byte-swizzled operand tiles start on 1024-byte boundaries");
 
 template <typename T>
 __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __grid_constant__ LinearParams p) {
