@@ -78,6 +78,8 @@ struct AttnSmem {
   static constexpr uint32_t bytes = flag_off + 16 + 1024;
   static_assert(kAttnComputeWarps * kMaxGroup * kHeadDim * 4 <= ST * kStageBytes, "ored must fit in the ring");
 };
+// Two 3-stage CTAs (plus the 1 KB the SM reserves for each) share an SM's 228 KB.
+static_assert(2 * (AttnSmem<3>::bytes + 1024) <= 228 * 1024, "the 3-stage ring must let two CTAs share an SM");
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
                                             int c3, uint32_t bar, uint64_t policy) {
