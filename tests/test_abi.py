@@ -127,3 +127,64 @@ def test_linear_split_argument_checks():
         runtime.linear_split(x, y, None, torch.zeros(32, 64, dtype=torch.float16))  # K mismatch
     with pytest.raises(RuntimeError):
         runtime.linear_split(x, y, None, torch.zeros(64, 64, dtype=torch.float32))  # dtype mismatch
+
+
+def _status(fn, *args):
+    from directaccesskernel_b200 import _lib
+
+    st = fn(*args)
+    return st, _lib.LIB.dak_last_error_message().decode()
+
+
+def test_decode_op_argument_checks_fail_before_any_launch():
+    """The decode-step entry points reject bad arguments with a status code and
+    a message, before touching the device (no GPU here)."""
+    from directaccesskernel_b200 import _lib
+
+    L = _lib.LIB
+    buf = ctypes.c_void_p(0x10000)  # never dereferenced: every call below fails its checks first
+    assert _status(L.dak_rmsnorm, buf, None, buf, buf, None, 4, 64, 64, 1e-5, 99, None)[0] == _lib.DAK_ERR_UNSUPPORTED
+    st, msg = _status(L.dak_rmsnorm, None, None, buf, buf, None, 4, 64, 64, 1e-5, _lib.DTYPE_F16, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "rmsnorm" in msg
+    st, msg = _status(L.dak_rmsnorm, buf, buf, buf, buf, None, 4, 64, 64, 1e-5, _lib.DTYPE_F16, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "residual" in msg
+    st, msg = _status(L.dak_rope_qk, buf, 3 * 128, buf, buf, buf, buf, buf, 2, 1, 1, 127, _lib.DTYPE_F16, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "head_dim" in msg
+    st, msg = _status(L.dak_rope_qk, buf, 100, buf, buf, buf, buf, buf, 2, 1, 1, 128, _lib.DTYPE_BF16, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "stride" in msg
+    st, msg = _status(L.dak_silu_mul, buf, 100, buf, 4, 64, _lib.DTYPE_F16, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "silu_mul" in msg
+    st, msg = _status(L.dak_rmsnorm_allreduce, None, buf, buf, buf, 4, 64, 64, 1e-5, _lib.DTYPE_F16, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "rmsnorm_allreduce" in msg
+
+
+def test_allreduce_and_kv_append_argument_checks():
+    from directaccesskernel_b200 import _lib
+
+    L = _lib.LIB
+    ar = _lib.AllReduceArgs()
+    ar.world, ar.rank = 9, 0
+    lin = _lib.LinearArgs()
+    st, msg = _status(L.dak_linear_split_allreduce, ctypes.byref(lin), ctypes.byref(ar), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "world" in msg
+    ar.world = 2
+    st, msg = _status(L.dak_linear_split_allreduce, ctypes.byref(lin), ctypes.byref(ar), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "required" in msg
+
+    a = _lib.KvAppendArgs()
+    a.batch, a.kv_heads, a.head_dim, a.page_size, a.max_pages, a.dtype = 2, 1, 128, 16, 4, _lib.DTYPE_F16
+    st, msg = _status(L.dak_kv_append_paged, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "required" in msg
+    a.k_new = a.v_new = a.block_table = a.positions = 0x10000
+    a.table_stride = 2
+    st, msg = _status(L.dak_kv_append_paged, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "table_stride" in msg
+    a.table_stride = 4
+    a.dev_pages = 3  # a page count without pools
+    st, msg = _status(L.dak_kv_append_paged, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "pools" in msg
+    a.head_dim = 12
+    st, msg = _status(L.dak_kv_append_paged, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_ALIGNMENT and "head_dim" in msg
+    a.dtype = _lib.DTYPE_F32
+    assert _status(L.dak_kv_append_paged, ctypes.byref(a), None)[0] == _lib.DAK_ERR_UNSUPPORTED
