@@ -84,7 +84,7 @@ class AttnPagedArgs(ctypes.Structure):
         ("partial_o", c_vp), ("partial_ml", c_vp),
         ("batch", c_int), ("num_q_heads", c_int), ("num_kv_heads", c_int), ("head_dim", c_int),
         ("page_size", c_int), ("max_seq_len", c_int), ("split_size", c_int),
-        ("scaling", ctypes.c_float), ("dtype", c_int),
+        ("scaling", ctypes.c_float), ("dtype", c_int), ("dev_pages", c_i64), ("host_pages", c_i64),
     ]
 
 

@@ -272,6 +272,9 @@ def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_de
     a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim = B, Hq, Hkv, HEAD_DIM
     a.page_size, a.max_seq_len, a.split_size = page_size, max_seq_len, split_size
     a.scaling, a.dtype = float(scaling), dak_dtype(query.dtype)
+    # Page counts let the kernel bound every table entry (out of range: zeros + error word).
+    a.dev_pages = k_pool_dev.size(0) if k_pool_dev is not None else 0
+    a.host_pages = k_pool_host.size(0) if k_pool_host is not None else 0
     check(LIB.dak_attn_decode_paged(ctypes.byref(a), _stream_ptr()), "decode_paged")
     return out
 

@@ -58,6 +58,8 @@ struct alignas(64) AttnParams {
   float scaling;
   int *status;
   int pdl;                 // launched with programmatic stream serialization
+  int check_pages;         // paged mode: bound table entries by pages[]
+  long long pages[2];      // paged mode: pages in the [0] host, [1] device pool (0: no pool)
 };
 
 // Shared memory of a CTA with an ST-stage ring.  Below the default depth the
@@ -225,6 +227,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
                 loc.tier = v < 0 ? 0 : 1;
                 loc.slab = v < 0 ? (-1 - v) : v;
                 loc.row = 0;
+                if (p.check_pages && loc.slab >= p.pages[loc.tier]) {
+                  // Past the pool (or no pool): one past the tile map's last
+                  // page, so the copy reads zeros and still completes.
+                  atomicCAS(p.status, 0, DAK_ERR_INVALID_ARG);
+                  loc.slab = (int)max(1ll, p.pages[loc.tier]);
+                }
               } else {
                 loc = locate(p, b, c0 + pg * psz);
               }
@@ -642,18 +650,27 @@ int dak_attn_decode_paged(const dak_attn_paged_args *a, void *stream) {
   p.pdl = decode_pdl_enabled() ? 1 : 0;
   const long long hs = (long long)a->page_size * kHeadDim;      // head stride in a page
   const long long ps = hs * a->num_kv_heads;                     // page stride
-  // The pools' page counts are not passed; the maps cover the largest page
-  // index a 31-bit table entry can name.
+  if (!a->k_pool_dev && !a->k_pool_host) return fail(DAK_ERR_INVALID_ARG, "no KV pool given");
+  if (a->dev_pages < 0 || a->host_pages < 0) return fail(DAK_ERR_INVALID_ARG, "page counts must not be negative");
+  // With page counts, each map covers exactly its pool and the kernel bounds
+  // every table entry; a tier without a pool gets a one-page map over the
+  // other tier's pool that no entry reaches.  Without them, the maps cover the
+  // largest page index a 31-bit table entry can name and entries are trusted.
+  p.check_pages = (a->dev_pages > 0 || a->host_pages > 0) ? 1 : 0;
+  p.pages[0] = a->k_pool_host ? a->host_pages : 0;
+  p.pages[1] = a->k_pool_dev ? a->dev_pages : 0;
   const long long max_pages = 1ll << 24;
   const void *pools[4] = {a->k_pool_host, a->v_pool_host, a->k_pool_dev, a->v_pool_dev};
   for (int i = 0; i < 4; ++i) {
-    if (!pools[i]) continue;
-    if ((reinterpret_cast<uintptr_t>(pools[i]) & 15u) != 0) return fail(DAK_ERR_ALIGNMENT, "KV pools must be 16-byte aligned");
-    CUtensorMap *m = (i % 2 == 0) ? &p.kmap[i / 2] : &p.vmap[i / 2];
-    if ((st = kv_map(m, pools[i], a->dtype, a->page_size, a->num_kv_heads, max_pages, kHeadDim, hs, ps, a->page_size)))
+    const int tier = i < 2 ? 0 : 1;
+    const void *base = pools[i] ? pools[i] : (p.check_pages ? pools[i ^ 2] : nullptr);
+    if (!base) continue;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return fail(DAK_ERR_ALIGNMENT, "KV pools must be 16-byte aligned");
+    const long long slabs = p.check_pages ? std::max(1ll, p.pages[tier]) : max_pages;
+    CUtensorMap *m = (i % 2 == 0) ? &p.kmap[tier] : &p.vmap[tier];
+    if ((st = kv_map(m, base, a->dtype, a->page_size, a->num_kv_heads, slabs, kHeadDim, hs, ps, a->page_size)))
       return st;
   }
-  if (!a->k_pool_dev && !a->k_pool_host) return fail(DAK_ERR_INVALID_ARG, "no KV pool given");
   const int splits = (a->max_seq_len + a->split_size - 1) / a->split_size;
   if (splits > 1 && (!a->partial_o || !a->partial_ml))
     return fail(DAK_ERR_INVALID_ARG, "partial_o and partial_ml scratch are required when max_seq_len > split_size");

@@ -188,3 +188,40 @@ def test_allreduce_and_kv_append_argument_checks():
     assert st == _lib.DAK_ERR_ALIGNMENT and "head_dim" in msg
     a.dtype = _lib.DTYPE_F32
     assert _status(L.dak_kv_append_paged, ctypes.byref(a), None)[0] == _lib.DAK_ERR_UNSUPPORTED
+
+
+STRUCTS = {"Constants": "dak_constants", "LinearArgs": "dak_linear_args", "AllReduceArgs": "dak_allreduce_args",
+           "AttnDecodeArgs": "dak_attn_decode_args", "AttnPagedArgs": "dak_attn_paged_args",
+           "KvAppendArgs": "dak_kv_append_args"}
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """Every ctypes mirror of an argument struct has the size and field offsets
+    that a C compiler gives the struct of include/dak_b200.h."""
+    import shutil
+    import subprocess
+
+    from directaccesskernel_b200 import _lib
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "dak_b200.h"', "int main(void) {"]
+    for py, c in STRUCTS.items():
+        lines.append(f'  printf("{py} size %zu\\n", sizeof({c}));')
+        for name, *_ in getattr(_lib, py)._fields_:
+            lines.append(f'  printf("{py} {name} %zu\\n", offsetof({c}, {name}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(REPO / "include"), "-o", str(exe), str(src)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        py, name, val = line.split()
+        got[(py, name)] = int(val)
+    for py in STRUCTS:
+        cls = getattr(_lib, py)
+        assert got[(py, "size")] == ctypes.sizeof(cls), py
+        for name, *_ in cls._fields_:
+            assert got[(py, name)] == getattr(cls, name).offset, (py, name)
