@@ -361,7 +361,8 @@ DAK_API int dak_silu_mul(const void *gate_up, int64_t ld, void *out, int rows, i
 
 /* ------------------------------------------------------------ diagnostics */
 /* Reads (and with clear != 0 resets) the device-side error word that kernels
- * set when a bounded wait times out.  Synchronizes the current device. */
+ * set when a bounded wait times out (DAK_ERR_TIMEOUT) or a block-table entry
+ * is out of range (DAK_ERR_INVALID_ARG).  Synchronizes the current device. */
 DAK_API int dak_device_status(int clear, int *status_out);
 
 /* Failure-path self test (no reference counterpart): launches one CTA whose
