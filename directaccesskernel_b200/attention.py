@@ -26,6 +26,7 @@ import torch
 from . import _lib
 from ._lib import LIB, check
 from .runtime import dak_dtype
+from .trace import traced
 
 HEAD_DIM = 128
 DEFAULT_SPLIT_SIZE = 256
@@ -108,6 +109,7 @@ def _check_mask(mask, query, seq_len) -> None:
         raise RuntimeError("attention_mask last dimension must be contiguous")
 
 
+@traced
 def decode(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, key_host: torch.Tensor | None = None,
            value_host: torch.Tensor | None = None, host_size: int = 0, attention_mask: torch.Tensor | None = None,
            scaling: float = 1.0, split_size: int = DEFAULT_SPLIT_SIZE, *, partial_o: torch.Tensor | None = None,
@@ -207,6 +209,7 @@ def auto_split_size(batch: int, kv_heads: int, max_seq_len: int, num_sms: int | 
     return best
 
 
+@traced
 def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_dev: torch.Tensor | None,
                  k_pool_host: torch.Tensor | None, v_pool_host: torch.Tensor | None, block_table: torch.Tensor,
                  seq_lens: torch.Tensor, scaling: float, split_size: int | None = None, *,
@@ -279,6 +282,7 @@ def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_de
     return out
 
 
+@traced
 def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.Tensor | None,
                     v_pool_dev: torch.Tensor | None, k_pool_host: torch.Tensor | None,
                     v_pool_host: torch.Tensor | None, block_table: torch.Tensor, positions: torch.Tensor) -> None:
@@ -350,6 +354,7 @@ def _prefill_attention(module, query, key, value, attention_mask, dropout, scali
     return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling, **kwargs)
 
 
+@traced
 def opt_attention_forward(module, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                           attention_mask: torch.Tensor | None, dropout: float = 0.0, scaling: float | None = None,
                           **kwargs):

@@ -8,6 +8,7 @@ import torch
 
 from ._lib import LIB, check
 from .runtime import dak_dtype
+from .trace import traced
 
 
 def _stream() -> int:
@@ -22,6 +23,7 @@ def _check16(*ts):
             raise RuntimeError("decode ops need a contiguous last dimension")
 
 
+@traced
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
             out: torch.Tensor | None = None) -> torch.Tensor:
     """RMSNorm of x [rows, cols]; with ``residual``, first x + residual, written back
@@ -42,6 +44,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.T
     return out
 
 
+@traced
 def rope_qk(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, q_heads: int, kv_heads: int,
             head_dim: int, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor) -> None:
     """Rotary q/k of a fused qkv [B, (q_heads + 2 kv_heads) * head_dim] into q_out
@@ -56,6 +59,7 @@ def rope_qk(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, 
                           dak_dtype(qkv.dtype), _stream()), "rope_qk")
 
 
+@traced
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """silu(gate) * up for gate_up [rows, 2 * cols] = [gate | up]."""
     _check16(gate_up)

@@ -21,6 +21,7 @@ import torch
 
 from . import _lib
 from ._lib import LIB, check
+from .trace import traced
 
 _C = _lib.constants()
 
@@ -111,12 +112,14 @@ def tensormap_replace_address(desc: torch.Tensor, data: torch.Tensor) -> None:
     check(LIB.dak_tensormap_replace_address(_desc_ptr(desc, "desc"), data.data_ptr()), "tensormap_replace_address")
 
 
+@traced
 def gemv(a_desc, b_desc, c_desc, M: int, N: int, K: int, num_copy_blocks: int, smem_size: int, sms_per_row: int) -> None:
     """src/torch_runtime.cu:201-221: C[N, M] = B[N, K] @ A[K, M]."""
     check(LIB.dak_gemv(_desc_ptr(a_desc, "a_desc"), _desc_ptr(b_desc, "b_desc"), _desc_ptr(c_desc, "c_desc"),
                        M, N, K, num_copy_blocks, smem_size, sms_per_row, _stream_ptr()), "gemv")
 
 
+@traced
 def gemv_horizontal(a_desc_h, a_desc_d, b_desc, c_desc, h_M: int, d_M: int, N: int, K: int,
                     num_copy_blocks: int, num_copy_host_blocks: int, smem_size: int,
                     h_sms_per_row: int, d_sms_per_row: int) -> None:
@@ -127,12 +130,14 @@ def gemv_horizontal(a_desc_h, a_desc_d, b_desc, c_desc, h_M: int, d_M: int, N: i
         num_copy_host_blocks, smem_size, h_sms_per_row, d_sms_per_row, _stream_ptr()), "gemv_horizontal")
 
 
+@traced
 def gemv_multicast(a_desc, b_desc, c_desc, M, N, K, num_copy_blocks, smem_size, sms_per_row) -> None:
     """src/torch_runtime.cu:313-336 (served by the tcgen05 kernel, no multicast)."""
     check(LIB.dak_gemv_multicast(_desc_ptr(a_desc, "a_desc"), _desc_ptr(b_desc, "b_desc"), _desc_ptr(c_desc, "c_desc"),
                                  M, N, K, num_copy_blocks, smem_size, sms_per_row, _stream_ptr()), "gemv_multicast")
 
 
+@traced
 def gemv_multicast_prefill(a_desc, b_desc, c_desc, M, N, K, num_copy_blocks, smem_size, sms_per_row) -> None:
     """src/torch_runtime.cu:338-361."""
     check(LIB.dak_gemv_multicast_prefill(_desc_ptr(a_desc, "a_desc"), _desc_ptr(b_desc, "b_desc"),
@@ -140,6 +145,7 @@ def gemv_multicast_prefill(a_desc, b_desc, c_desc, M, N, K, num_copy_blocks, sme
                                          sms_per_row, _stream_ptr()), "gemv_multicast_prefill")
 
 
+@traced
 def gemv_horizontal_multicast(h_a_desc, d_a_desc, b_desc, c_desc, h_M, d_M, N, K, num_copy_blocks,
                               num_copy_host_blocks, smem_size, h_sms_per_row, d_sms_per_row) -> None:
     """src/torch_runtime.cu:247-278."""
@@ -149,6 +155,7 @@ def gemv_horizontal_multicast(h_a_desc, d_a_desc, b_desc, c_desc, h_M, d_M, N, K
         num_copy_host_blocks, smem_size, h_sms_per_row, d_sms_per_row, _stream_ptr()), "gemv_horizontal_multicast")
 
 
+@traced
 def gemv_horizontal_multicast_prefill(h_a_desc, d_a_desc, b_desc, c_desc, h_M, d_M, N, K, num_copy_blocks,
                                       num_copy_host_blocks, smem_size, h_sms_per_row, d_sms_per_row) -> None:
     """src/torch_runtime.cu:280-311."""
@@ -176,6 +183,7 @@ def _i64(v) -> int:
     return int(v)
 
 
+@traced
 def linear_split(x: torch.Tensor, y: torch.Tensor, w_host: torch.Tensor | None, w_dev: torch.Tensor | None,
                  host_col_offset: int = 0, dev_col_offset: int | None = None, *, host_ctas: int = 0,
                  dev_ctas: int = 0, host_ksplit: int = 0, dev_ksplit: int = 0, path: int = _lib.PATH_AUTO,

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import checksum, cuda_to, gen, golden_json, golden_npz
+from conftest import REPO, checksum, cuda_to, gen, golden_json, golden_npz
 
 
 def test_descriptor_arguments_match_reference():
@@ -240,3 +240,22 @@ def test_auto_split_size():
 
     s = auto_split_size(8, 8, 32768, num_sms=148)
     assert s % 64 == 0 and 8 * 8 * math.ceil(32768 / s) >= 4 * 148 * 0.9
+
+
+def test_nvtx_tracing_is_opt_in():
+    """DAK_B200_NVTX=1 wraps the launch entry points in NVTX ranges; without it
+    they are the plain functions (no per-call cost)."""
+    import os
+    import subprocess
+    import sys
+
+    code = ("from directaccesskernel_b200 import runtime, attention, decode_ops;"
+            "fs = [runtime.gemv_horizontal, runtime.linear_split, attention.decode_paged,"
+            " attention.kv_append_paged, decode_ops.rmsnorm];"
+            "print(sum(hasattr(f, '__wrapped__') for f in fs))")
+    env = dict(os.environ)
+    for flag, want in (("1", "5"), ("0", "0")):
+        env["DAK_B200_NVTX"] = flag
+        out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, cwd=REPO)
+        assert out.returncode == 0, out.stderr
+        assert out.stdout.strip() == want
