@@ -1,6 +1,6 @@
 // dak_linear_mma.cu - split-tier offloaded linear on the 5th-generation tensor
 // cores (tcgen05.mma kind::f16, FP32 accumulators in TMEM), for batched decode
-// and prefill (ntok 9..256).
+// and prefill (from 3 tokens under the automatic path choice, 256 per launch).
 //
 // Replaces the reference's wgmma kernels `gemv_multicast`,
 // `gemv_horizontal_multicast` and their `_prefill` variants
