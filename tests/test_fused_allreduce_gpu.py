@@ -24,7 +24,7 @@ def _rel(a, b):
     return float((a.float() - b.float()).abs().max() / b.float().abs().max())
 
 
-def _worker(rank, world, port, q, multicast):
+def _worker(rank, world, port, q, multicast, dtype=torch.float16):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -39,21 +39,21 @@ def _worker(rank, world, port, q, multicast):
 
         errs = []
         N, Kr = 4096, 1024
-        ar = SymmetricAllReduce(slot_elems=64 * N, multicast=multicast)
+        ar = SymmetricAllReduce(slot_elems=64 * N, multicast=multicast, dtype=dtype)
         g = torch.Generator(device="cuda").manual_seed(100 + rank)
-        w = (torch.randn(Kr, N, generator=g, device="cuda") * 0.02).half()  # this rank's [K_r, N] shard
+        w = (torch.randn(Kr, N, generator=g, device="cuda") * 0.02).to(dtype)  # this rank's [K_r, N] shard
         w_host = w[:, :1024].contiguous().cpu().pin_memory()
         w_dev = w[:, 1024:].contiguous()
         for ntok in (1, 32, 64, 32, 5):
-            x = torch.randn(ntok, Kr, generator=g, device="cuda").half()
-            y = torch.empty(ntok, N, dtype=torch.float16, device="cuda")
+            x = torch.randn(ntok, Kr, generator=g, device="cuda").to(dtype)
+            y = torch.empty(ntok, N, dtype=dtype, device="cuda")
             runtime.linear_split(x, y, w_host, w_dev, allreduce=ar)
             ref = (x.float() @ w.float()).contiguous()
             dist.all_reduce(ref)
             errs.append(_rel(y, ref))
         # CUDA graph: three fused calls captured, replayed twice with new inputs.
-        xs = [torch.randn(32, Kr, generator=g, device="cuda").half() for _ in range(3)]
-        ys = [torch.empty(32, N, dtype=torch.float16, device="cuda") for _ in range(3)]
+        xs = [torch.randn(32, Kr, generator=g, device="cuda").to(dtype) for _ in range(3)]
+        ys = [torch.empty(32, N, dtype=dtype, device="cuda") for _ in range(3)]
         for i in range(3):
             runtime.linear_split(xs[i], ys[i], w_host, w_dev, allreduce=ar)
         torch.cuda.synchronize()
@@ -63,7 +63,7 @@ def _worker(rank, world, port, q, multicast):
                 runtime.linear_split(xs[i], ys[i], w_host, w_dev, allreduce=ar)
         for _ in range(2):
             for i in range(3):
-                xs[i].copy_(torch.randn(32, Kr, generator=g, device="cuda").half())
+                xs[i].copy_(torch.randn(32, Kr, generator=g, device="cuda").to(dtype))
             graph.replay()
             torch.cuda.synchronize()
             for i in range(3):
@@ -78,9 +78,10 @@ def _worker(rank, world, port, q, multicast):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("multicast", [False, True])
 @pytest.mark.parametrize("world", [1, 2])
-def test_fused_allreduce_matches_nccl(world, multicast):
+def test_fused_allreduce_matches_nccl(world, multicast, dtype):
     """Peer-store mode, and the multimem mode where the box offers multicast
     (the context falls back to peer stores otherwise; the mode is reported)."""
     if torch.cuda.device_count() < world:
@@ -90,7 +91,7 @@ def test_fused_allreduce_matches_nccl(world, multicast):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, multicast)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, multicast, dtype)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
