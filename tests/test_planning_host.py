@@ -74,3 +74,36 @@ def test_rank_shape_matches_a_tp8_rank():
     assert r.kv_bytes_per_rank(1, 32, 16384) == full.kv_bytes_per_rank(8, 32, 16384)
     with pytest.raises(ValueError):
         bench.rank_shape(full, 3)
+
+
+def _bench(args, env_extra=None, timeout=300):
+    import json
+    import os
+    import subprocess
+    import sys
+
+    from conftest import REPO
+
+    env = dict(os.environ, **(env_extra or {}))
+    r = subprocess.run([sys.executable, str(REPO / "bench.py"), *args], capture_output=True, text=True,
+                       timeout=timeout, env=env, cwd=REPO)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    return [json.loads(ln) for ln in lines]
+
+
+def test_reference_arm_prints_one_contract_line():
+    """`bench.py --impl reference` (the driver's reference arm): one JSON line on
+    this arm's metric and unit, with the CPU baseline it timed and an e2e entry
+    without host/device copies."""
+    (line,) = _bench(["--impl", "reference", "--steps", "1", "--warmup", "0"])
+    assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["higher_is_better"] is True
+    assert line["metric"].startswith("offloaded GEMV effective weight GB/s")
+    assert line["value"] > 0 and line["steps"] == 1
+    cpu = line["cpu_baseline"]
+    assert cpu["kind"] == "port" and cpu["cores"] >= 1 and cpu["value"] == line["value"] and cpu["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_runs_on_rank_zero_only():
+    assert _bench(["--impl", "reference", "--steps", "1", "--warmup", "0"], {"RANK": "1", "WORLD_SIZE": "2"}) == []
