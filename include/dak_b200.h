@@ -282,11 +282,12 @@ DAK_API int dak_attn_decode_noalloc(const dak_attn_decode_args *args, void *stre
 /* Paged form: KV pages of page_size tokens live in two pools, one in HBM and
  * one in pinned host memory, both laid out [pages, Hkv, page_size, D].
  * block_table[b * bt_stride + j] names page j of sequence b: a value v >= 0 is
- * device page v, v < 0 is host page (-1 - v).  With dev_pages / host_pages
- * given (either > 0), an entry past its pool, or naming a tier without a
- * pool, reads zeros and is recorded in the device error word
- * (DAK_ERR_INVALID_ARG); with both 0 the entries are trusted.  No reference
- * counterpart: the reference has only the batch-split form above. */
+ * device page v, v < 0 is host page (-1 - v).  When either of dev_pages /
+ * host_pages is > 0, both are the pools' page counts (0 = that pool is empty
+ * or absent) and every entry is bounded by them: an entry past its pool reads
+ * zeros and is recorded in the device error word (DAK_ERR_INVALID_ARG).  With
+ * both 0 the entries are trusted.  No reference counterpart: the reference has
+ * only the batch-split form above. */
 typedef struct dak_attn_paged_args {
   const void *query;        /* [B, Hq, D]                                   */
   int64_t q_stride_b, q_stride_h;
@@ -302,7 +303,7 @@ typedef struct dak_attn_paged_args {
   int split_size;           /* tokens per split, multiple of page_size     */
   float scaling;
   int dtype;
-  int64_t dev_pages, host_pages;  /* pages in each pool (0: unchecked)     */
+  int64_t dev_pages, host_pages;  /* pages in each pool; both 0: unchecked */
 } dak_attn_paged_args;
 DAK_API int dak_attn_decode_paged(const dak_attn_paged_args *args, void *stream);
 
