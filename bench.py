@@ -65,6 +65,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
     ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
     ap.add_argument("--ctx", type=int, default=16384, help="llama70b: context tokens per sequence")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="llama70b: after the timed region, one eager step with CUDA events around every op group "
+                         "(per-op milliseconds in the JSON line)")
     ap.add_argument("--rank-of-tp", type=int, default=1,
                     help="llama70b on 1 GPU: build one rank of a TP-N decoder (heads, KV heads, FFN and vocabulary "
                          "divided by N) to profile its kernels on one GPU; there is no all-reduce")
@@ -737,7 +740,9 @@ def run_llama70b(args, torch, rank, world):
         shape = rank_shape(shape, emulated)
     B, ctx = args.batch, args.ctx
     W, K = max(3, args.warmup), args.steps
-    max_ctx = ctx + W + K + 4
+    # Room for every token the run appends: warm-up, timed and end-to-end steps,
+    # the profiled step, and the capture's warm-up step (undone, but written).
+    max_ctx = ctx + W + 2 * K + 4
     budget_gb = 60.0 if args.hbm_budget_gb is None else args.hbm_budget_gb
     frac = (args.host_fraction if args.host_fraction is not None
             else budget_fraction(shape, world, B, max_ctx, int(budget_gb * 1e9)))
@@ -803,6 +808,8 @@ def run_llama70b(args, torch, rank, world):
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = times.tolist()
     dec.release()
+    # Every rank runs the profiled step: it holds the same collectives as a step.
+    breakdown = dec.profile_step() if args.breakdown else None
     dec_ar_mode = dec.ar.mode if dec.ar is not None else None
     fused = fused and dec_ar_mode is not None
     if status != 0:
@@ -864,6 +871,9 @@ def run_llama70b(args, torch, rank, world):
                 "d2h_bytes_per_step": 8 * B},
         "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
         **({"cpu_baseline": cpu} if cpu is not None else {}),
+        **({"breakdown_ms": breakdown,
+            "breakdown_basis": "rank 0, one eager step outside the timed region, CUDA events around each op group "
+                               "(kernels serialized by the events)"} if breakdown is not None else {}),
     }
 
 

@@ -23,6 +23,7 @@ the element-wise steps are the fused kernels of ``decode_ops``.
 """
 from __future__ import annotations
 
+import contextlib
 import dataclasses
 import math
 
@@ -322,35 +323,51 @@ class TPLlamaDecoder(nn.Module):
         from .decode_ops import rmsnorm, rope_qk, silu_mul
 
         s, B, d = self.s, self.B, self.s.head_dim
-        torch.add(self.pos, 1, out=self.seq_lens)
-        self.hidden.copy_(self.embed[self.ids])
+        t = self._span
+        with t("embed"):
+            torch.add(self.pos, 1, out=self.seq_lens)
+            self.hidden.copy_(self.embed[self.ids])
         qd = self.hq * d
         scale = 1.0 / math.sqrt(d)
-        x = rmsnorm(self.hidden, self.layers[0].in_w, s.eps, out=self.x_buf)
+        with t("norm"):
+            x = rmsnorm(self.hidden, self.layers[0].in_w, s.eps, out=self.x_buf)
         for l, layer in enumerate(self.layers):
-            qkv = layer.qkv(x)
-            rope_qk(qkv, self.pos, self.inv_freq, self.hq, self.hkv, d, self.q_buf, self.k_buf, self.v_buf)
+            with t("qkv"):
+                qkv = layer.qkv(x)
+            with t("rope"):
+                rope_qk(qkv, self.pos, self.inv_freq, self.hq, self.hkv, d, self.q_buf, self.k_buf, self.v_buf)
             kdev, vdev, khost, vhost = self._pools(l)
-            kv_append_paged(self.k_buf, self.v_buf, kdev, vdev, khost, vhost, self.block_table, self.pos)
-            decode_paged(self.q_buf, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale, self.split,
-                         out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
-                         max_seq_len=self.max_ctx)
-            o = self._row_parallel(layer.o, self.attn_out.view(B, qd), self.o_buf)
-            x = self._add_norm(o, layer.post_w)
-            gu = layer.gate_up(x)
-            dn = self._row_parallel(layer.down, silu_mul(gu, out=self.act_buf), self.dn_buf)
+            with t("kv_append"):
+                kv_append_paged(self.k_buf, self.v_buf, kdev, vdev, khost, vhost, self.block_table, self.pos)
+            with t("attention"):
+                decode_paged(self.q_buf, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale,
+                             self.split, out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
+                             max_seq_len=self.max_ctx)
+            with t("o" if self.ar is not None else "o+allreduce"):
+                o = self._row_parallel(layer.o, self.attn_out.view(B, qd), self.o_buf)
+            with t("allreduce+norm" if self.ar is not None else "norm"):
+                x = self._add_norm(o, layer.post_w)
+            with t("gate_up"):
+                gu = layer.gate_up(x)
+            with t("silu"):
+                act = silu_mul(gu, out=self.act_buf)
+            with t("down" if self.ar is not None else "down+allreduce"):
+                dn = self._row_parallel(layer.down, act, self.dn_buf)
             nxt_w = self.layers[l + 1].in_w if l + 1 < len(self.layers) else self.final_w
-            x = self._add_norm(dn, nxt_w)
-        logits = self.lm_head(x)[:, :max(1, self.vocab_valid)]
-        val, idx = logits.float().max(dim=-1)
-        if self.world > 1:
-            pair = torch.stack([val, (idx + self.rank * self.vocab_r).float()], dim=-1)  # [B, 2]
-            allp = torch.empty(self.world, B, 2, dtype=pair.dtype, device=pair.device)
-            dist.all_gather_into_tensor(allp, pair, group=self.group)
-            best = allp[:, :, 0].argmax(dim=0)  # first maximum, as argmax over the full row
-            self.next_ids.copy_(allp[best, torch.arange(B, device=pair.device), 1].long())
-        else:
-            self.next_ids.copy_(idx)
+            with t("allreduce+norm" if self.ar is not None else "norm"):
+                x = self._add_norm(dn, nxt_w)
+        with t("lm_head"):
+            logits = self.lm_head(x)[:, :max(1, self.vocab_valid)]
+        with t("pick"):
+            val, idx = logits.float().max(dim=-1)
+            if self.world > 1:
+                pair = torch.stack([val, (idx + self.rank * self.vocab_r).float()], dim=-1)  # [B, 2]
+                allp = torch.empty(self.world, B, 2, dtype=pair.dtype, device=pair.device)
+                dist.all_gather_into_tensor(allp, pair, group=self.group)
+                best = allp[:, :, 0].argmax(dim=0)  # first maximum, as argmax over the full row
+                self.next_ids.copy_(allp[best, torch.arange(B, device=pair.device), 1].long())
+            else:
+                self.next_ids.copy_(idx)
         if keep_logits:
             if self.world > 1:
                 parts = torch.empty(self.world * B, self.vocab_r, dtype=logits.dtype, device=logits.device)
@@ -362,6 +379,40 @@ class TPLlamaDecoder(nn.Module):
             else:
                 self.logits_full = logits
         return self.next_ids
+
+    def _span(self, name: str):
+        """Timing scope of one op group of ``forward_step``: CUDA events around it
+        while ``profile_step`` runs, nothing otherwise (graph capture included)."""
+        timer = getattr(self, "_timer", None)
+        return timer(name) if timer is not None else contextlib.nullcontext()
+
+    @torch.inference_mode()
+    def profile_step(self) -> dict[str, float]:
+        """One eager decode step (plus the advance) with CUDA events around every op
+        group; returns milliseconds per group summed over the layers.  Events
+        between the kernels stop them from overlapping, so the sum exceeds a
+        graph replay's time; the shares show where a step goes."""
+        events = []
+
+        @contextlib.contextmanager
+        def timer(name):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            yield
+            e1.record()
+            events.append((name, e0, e1))
+
+        self._timer = timer
+        try:
+            self.forward_step()
+            self.advance()
+        finally:
+            self._timer = None
+        torch.cuda.synchronize()
+        out: dict[str, float] = {}
+        for name, e0, e1 in events:
+            out[name] = out.get(name, 0.0) + e0.elapsed_time(e1)
+        return {k: round(v, 4) for k, v in out.items()}
 
     def kernel_launches_per_step(self) -> int:
         """Launches of this library's kernels in one ``forward_step``: the first
