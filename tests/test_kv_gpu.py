@@ -5,6 +5,7 @@ device error word instead of being written."""
 from __future__ import annotations
 
 import math
+import os
 
 import numpy as np
 import pytest
@@ -149,3 +150,44 @@ def test_writer_matches_the_reference_pinned_static_cache():
             vb = oracle.paged_gather(vd, vh, table[b], S)
             assert np.array_equal(kb[:, KV_WRITTEN], d[f"k{layer}"][b][:, KV_WRITTEN])
             assert np.array_equal(vb[:, KV_WRITTEN], d[f"v{layer}"][b][:, KV_WRITTEN])
+
+
+@pytest.mark.skipif(os.environ.get("DAK_B200_TEST_PAGED_BOUNDS") != "1",
+                    reason="first run on a B200 is deliberate: set DAK_B200_TEST_PAGED_BOUNDS=1")
+@pytest.mark.parametrize("host_pool", [True, False])
+def test_paged_attention_bounds_table_entries(host_pool):
+    """A block-table entry past its pool, or naming a tier without a pool, reads
+    zeros and sets DAK_ERR_INVALID_ARG in the error word; the other pages are
+    read as usual."""
+    from directaccesskernel_b200 import _lib, runtime
+    from directaccesskernel_b200.attention import decode_paged
+
+    B, Hq, Hkv, P, D, npg = 2, 8, 2, 16, 128, 6
+    kd, vd, kh, vh = _pools(npg, npg, Hkv, P, D, seed=9)
+    if not host_pool:
+        kh = vh = None
+    table = np.array([[0, 1, npg, 2, 3, 4], [5, -1, -1 - npg, 0, 1, 2]], dtype=np.int32)
+    if not host_pool:
+        table[1] = [5, -1, 3, 0, 1, 2]  # -1 names a host page, and there is no host pool
+    bad = {(0, 2), (1, 1)} if not host_pool else {(0, 2), (1, 2)}
+    g = torch.Generator().manual_seed(4)
+    q = (torch.randn(B, Hq, D, generator=g) / math.sqrt(D)).half()
+    S = npg * P
+    runtime.device_status(True)
+    out = decode_paged(q.cuda(), kd, vd, kh, vh, torch.from_numpy(table).cuda(),
+                       torch.full((B,), S, dtype=torch.int32, device="cuda"), 1 / math.sqrt(D), 64)
+    assert runtime.device_status(True) == _lib.DAK_ERR_INVALID_ARG
+    kdn, vdn = kd.cpu().numpy(), vd.cpu().numpy()
+    khn = kh.numpy() if kh is not None else None
+    vhn = vh.numpy() if vh is not None else None
+    K = np.zeros((B, Hkv, S, D), np.float16)
+    V = np.zeros((B, Hkv, S, D), np.float16)
+    for b in range(B):
+        for j in range(npg):
+            if (b, j) in bad:
+                continue  # reads zeros
+            e = int(table[b, j])
+            K[b, :, j * P:(j + 1) * P] = kdn[e] if e >= 0 else khn[-1 - e]
+            V[b, :, j * P:(j + 1) * P] = vdn[e] if e >= 0 else vhn[-1 - e]
+    ref = oracle.decode_attention(q.numpy()[:, :, None, :], K, V, None, 1 / math.sqrt(D))[:, 0]
+    assert rel_err(out.float().cpu().numpy(), ref) < 2e-3
