@@ -717,46 +717,76 @@ namespace {
 constexpr size_t kNoAllocScratchFloats = size_t(2) << 20;  // 8 MiB
 static __device__ __align__(256) float g_attn_noalloc_scratch[kNoAllocScratchFloats];
 constexpr int kNoAllocMaxDevices = 64;
+// Where the array lives, per device, and in which context that was looked up:
+// the address belongs to the context's copy of the library's module, so a
+// different current context (another driver-API context, or the primary
+// context created again after cudaDeviceReset) is looked up again.
+struct NoAllocSlot {
+  uint64_t ctx = 0;
+  float *ptr = nullptr;
+};
 std::mutex g_noalloc_mu;
-float *g_noalloc_ptr[kNoAllocMaxDevices];
+NoAllocSlot g_noalloc[kNoAllocMaxDevices];
 }  // namespace
 }  // namespace dak
 
 extern "C" int dak_attn_decode_noalloc(const dak_attn_decode_args *args, void *stream) {
   using namespace dak;
   if (!args) return fail(DAK_ERR_INVALID_ARG, "args is null");
-  if (args->split_size <= 0 || args->seq_len <= 0 || args->batch <= 0 || args->num_q_heads <= 0 ||
-      args->head_dim <= 0)
-    return fail(DAK_ERR_INVALID_ARG, "batch, heads, head_dim, seq_len and split_size must be positive");
-  const size_t splits = ((size_t)args->seq_len + args->split_size - 1) / args->split_size;
-  const size_t rows = (size_t)args->batch * (size_t)args->num_q_heads * splits;
-  const size_t need = rows * ((size_t)args->head_dim + 2);
-  if (need > kNoAllocScratchFloats)
-    return fail(DAK_ERR_INVALID_ARG,
-                "dak_attn_decode_noalloc: batch x q_heads x splits x (head_dim + 2) = %zu floats exceeds "
-                "its built-in scratch of %zu floats (8 MiB); raise split_size or use dak_attn_decode",
-                need, kNoAllocScratchFloats);
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(DAK_ERR_UNSUPPORTED, "device %d out of range", dev);
-  float *scratch;
-  {
-    // First call on this device: look up where the array lives on it.  In host
-    // code the array's name is only a stand-in, never a device address.
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-      void *ptr = nullptr;
-      e = cudaGetSymbolAddress(&ptr, g_attn_noalloc_scratch);
-      if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(scratch)");
-      g_noalloc_ptr[dev] = static_cast<float *>(ptr);
-    }
-    scratch = g_noalloc_ptr[dev];
-  }
-  // Every partial (o, m, l) the merge reads is written earlier in the same
-  // call, so the array needs no clearing between calls.
+  int group, st;
+  if ((st = common_checks(args->batch, args->num_q_heads, args->num_kv_heads, args->head_dim, args->split_size,
+                          args->dtype, &group)))
+    return st;
+  if (args->seq_len <= 0) return fail(DAK_ERR_INVALID_ARG, "seq_len must be positive");
+  const size_t splits = ((size_t)args->seq_len + (size_t)args->split_size - 1) / (size_t)args->split_size;
   dak_attn_decode_args a = *args;
-  a.partial_o = scratch;
-  a.partial_ml = scratch + rows * (size_t)args->head_dim;
+  a.partial_o = nullptr;
+  a.partial_ml = nullptr;
+  if (splits > 1) {
+    // Each factor is below 2^31 and the limit is 2^21, so bounding the running
+    // product by the limit before every multiplication keeps it exact.
+    const size_t per_row = (size_t)args->head_dim + 2;
+    size_t need = per_row;
+    const size_t factors[3] = {(size_t)args->batch, (size_t)args->num_q_heads, splits};
+    for (size_t f : factors) {
+      if (need > kNoAllocScratchFloats / f) {
+        need = kNoAllocScratchFloats + 1;
+        break;
+      }
+      need *= f;
+    }
+    if (need > kNoAllocScratchFloats)
+      return fail(DAK_ERR_INVALID_ARG,
+                  "dak_attn_decode_noalloc: batch x q_heads x splits x (head_dim + 2) exceeds its built-in "
+                  "scratch of %zu floats (8 MiB); raise split_size or use dak_attn_decode",
+                  kNoAllocScratchFloats);
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(DAK_ERR_UNSUPPORTED, "device %d out of range", dev);
+    const uint64_t ctx = current_context_id();
+    float *scratch;
+    {
+      // First call in this device's current context: look up where the array
+      // lives there.  In host code the array's name is only a stand-in, never
+      // a device address.
+      std::lock_guard<std::mutex> lk(g_noalloc_mu);
+      NoAllocSlot &slot = g_noalloc[dev];
+      if (!slot.ptr || ctx == 0 || slot.ctx != ctx) {
+        void *ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_attn_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(scratch)");
+        slot.ptr = static_cast<float *>(ptr);
+        slot.ctx = ctx ? ctx : current_context_id();
+      }
+      scratch = slot.ptr;
+    }
+    // Every partial (o, m, l) the merge reads is written earlier in the same
+    // call, so the array needs no clearing between calls.
+    const size_t rows = (size_t)args->batch * (size_t)args->num_q_heads * splits;
+    a.partial_o = scratch;
+    a.partial_ml = scratch + rows * (size_t)args->head_dim;
+  }
+  // With one split the kernel writes the output directly and uses no scratch.
   return dak_attn_decode(&a, stream);
 }

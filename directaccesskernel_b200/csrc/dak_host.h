@@ -17,7 +17,11 @@ int fail(int code, const char *fmt, ...);
 // Maps a CUDA runtime error to DAK_ERR_CUDA with its text (or DAK_OK).
 int cuda_status(cudaError_t e, const char *what);
 
-// Device address of the kernels' error word on the current device.
+// Identity of the CUDA context current on the calling thread (0 = none); unique
+// for the life of the process.  Per-device state that holds device addresses
+// or kernel attributes is set up again when it changes.
+uint64_t current_context_id();
+// Device address of the kernels' error word in the current context.
 int *device_status_word();
 // DAK_OK if `p` is memory of the current device or pinned host memory.
 int check_gpu_accessible(const void *p, const char *what);

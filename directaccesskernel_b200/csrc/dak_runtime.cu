@@ -45,11 +45,42 @@ int cuda_status(cudaError_t e, const char *what) {
 }
 
 // -------------------------------------------------------- per-device state
+// Identity of the CUDA context that is current on the calling thread (the
+// runtime's primary context, or one that a C-ABI host made current through
+// the driver API), or 0 when none is.  cuCtxGetId numbers contexts uniquely
+// for the life of the process, so a context created after cudaDeviceReset
+// gets a new identity even if its handle is reused.  Device addresses of the
+// library's `__device__` arrays and kernel attributes belong to one context,
+// so the state below is set up again whenever the current context's identity
+// differs from the one it was set up in.
+uint64_t current_context_id() {
+  using CtxGetCurrent = CUresult (*)(CUcontext *);
+  using CtxGetId = CUresult (*)(CUcontext, unsigned long long *);
+  static const std::pair<CtxGetCurrent, CtxGetId> fn = [] {
+    auto entry = [](const char *name) -> void * {
+      void *p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPointByVersion(name, &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess)
+        return nullptr;
+      return p;
+    };
+    return std::make_pair(reinterpret_cast<CtxGetCurrent>(entry("cuCtxGetCurrent")),
+                          reinterpret_cast<CtxGetId>(entry("cuCtxGetId")));
+  }();
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!fn.first || !fn.second || fn.first(&ctx) != CUDA_SUCCESS || !ctx || fn.second(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return (uint64_t)id + 1;  // never 0 for a live context
+}
+
 namespace {
 constexpr int kMaxDevices = 64;
 
 struct DeviceInfo {
   bool ready = false;
+  uint64_t ctx = 0;  // identity of the context the entry was set up in
   int num_sms = 0;
   int max_smem_optin = 0;
   int *status = nullptr;
@@ -68,14 +99,19 @@ int device_info(DeviceInfo **out) {
   int dev;
   int st = current_device(&dev);
   if (st) return st;
+  const uint64_t ctx = current_context_id();
   std::lock_guard<std::mutex> lk(g_dev_mu);
   DeviceInfo &d = g_dev[dev];
-  if (!d.ready) {
+  // No context yet means the runtime has not made one current: the symbol
+  // lookup below creates it, and the entry records it afterwards.
+  if (!d.ready || ctx == 0 || ctx != d.ctx) {
+    d.ready = false;
     cudaError_t e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
       e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void **>(&d.status), g_dak_status);
     if (e != cudaSuccess) return cuda_status(e, "device query");
+    d.ctx = ctx ? ctx : current_context_id();
     d.ready = true;
   }
   *out = &d;
@@ -90,17 +126,14 @@ int *device_status_word() {
 
 cudaError_t prepare_kernel_attributes(const void *kern) {
   static std::mutex mu;
-  static std::set<std::pair<int, const void *>> done;
+  static std::set<std::pair<uint64_t, const void *>> done;  // (context identity, kernel)
   DeviceInfo *d = nullptr;
   if (device_info(&d) != DAK_OK) return cudaErrorInvalidDevice;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lk(mu);
-  if (done.count({dev, kern})) return cudaSuccess;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->max_smem_optin);
+  if (d->ctx && done.count({d->ctx, kern})) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->max_smem_optin);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e == cudaSuccess) done.insert({dev, kern});
+  if (e == cudaSuccess && d->ctx) done.insert({d->ctx, kern});
   return e;
 }
 

@@ -270,8 +270,12 @@ DAK_API int dak_attn_decode(const dak_attn_decode_args *args, void *stream);
  * ignored.  The split-KV partials go to an 8 MiB array inside the library,
  * held on every GPU that loads it until the process exits, so
  * batch * num_q_heads * ceil(seq_len / split_size) * (head_dim + 2) must not
- * exceed 2,097,152 floats; larger calls fail with DAK_ERR_INVALID_ARG.  The
- * first call on a device looks up the array's address there, so make that
+ * exceed 2,097,152 floats; larger calls fail with DAK_ERR_INVALID_ARG.  A call
+ * with one split (seq_len <= split_size) writes the output directly, uses no
+ * scratch and has no such limit.  The first call in each CUDA context of a
+ * device (the runtime's primary context, a context the host made current
+ * through the driver API, or the primary context created again after
+ * cudaDeviceReset) looks up the array's address in that context, so make that
  * first call before any stream capture.  All calls share the one array:
  * calls that can overlap on the GPU (different streams, different threads)
  * race on it and must be serialized by the caller.  The array keeps the last
