@@ -5,7 +5,6 @@ device error word instead of being written."""
 from __future__ import annotations
 
 import math
-import os
 
 import numpy as np
 import pytest
@@ -152,8 +151,6 @@ def test_writer_matches_the_reference_pinned_static_cache():
             assert np.array_equal(vb[:, KV_WRITTEN], d[f"v{layer}"][b][:, KV_WRITTEN])
 
 
-@pytest.mark.skipif(os.environ.get("DAK_B200_TEST_PAGED_BOUNDS") != "1",
-                    reason="first run on a B200 is deliberate: set DAK_B200_TEST_PAGED_BOUNDS=1")
 @pytest.mark.parametrize("host_pool", [True, False])
 def test_paged_attention_bounds_table_entries(host_pool):
     """A block-table entry past its pool, or naming a tier without a pool, reads
