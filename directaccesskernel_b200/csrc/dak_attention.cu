@@ -9,8 +9,8 @@
 // Here:
 //   * one CTA per (batch, KV head, split) serves all G = Hq/Hkv query heads of
 //     the GQA group, so every KV byte crosses the host link or HBM once;
-//   * K/V arrive as 64-token chunks through a 4-stage ring (3 stages and two
-//     CTAs per SM with DAK_B200_ATTN_STAGES=3) filled by TMA 4-D
+//   * K/V arrive as 64-token chunks through a 3-stage ring (two CTAs per SM,
+//     so one CTA's start-up overlaps the other's stream) filled by TMA 4-D
 //     tile loads (128-byte swizzle) issued by one producer warp; each chunk is
 //     made of pages (64 tokens of one row in the reference's [B, H, S, D]
 //     layout, or page_size-token pages of a paged pool), and each page picks
@@ -31,7 +31,7 @@ namespace {
 
 constexpr int kHeadDim = 128;
 constexpr int kChunk = 64;          // tokens per pipeline stage
-constexpr int kAttnStages = 4;      // default ring depth (one CTA per SM)
+constexpr int kAttnStages = 3;      // ring depth: two CTAs share an SM
 constexpr int kAttnComputeWarps = 4;
 constexpr int kAttnThreads = (kAttnComputeWarps + 1) * 32;
 constexpr int kMaxGroup = 8;
@@ -62,17 +62,16 @@ struct alignas(64) AttnParams {
   long long pages[2];      // paged mode: pages in the [0] host, [1] device pool (0: no pool)
 };
 
-// Shared memory of a CTA with an ST-stage ring.  Below the default depth the
-// warps' partial outputs (ored, 4 x G x 128 FP32), merged after the last chunk
-// has been consumed, reuse the ring: with 3 stages a CTA needs about 98 KB and
-// two CTAs share an SM, so one CTA's start-up overlaps the other's stream.
+// Shared memory of a CTA with an ST-stage ring.  The warps' partial outputs
+// (ored, 4 x G x 128 FP32), merged after the last chunk has been consumed,
+// reuse the ring, so a 3-stage CTA needs about 98 KB and two CTAs share an
+// SM: one CTA's start-up (barrier set-up, first TMA round trip) overlaps the
+// other's stream.
 template <int ST>
 struct AttnSmem {
-  static constexpr bool ored_in_ring = ST < kAttnStages;
   static constexpr uint32_t kv_off = 0;
-  static constexpr uint32_t ored_off = ored_in_ring ? kv_off : kv_off + ST * kStageBytes;  // 4 x G x 128
-  static constexpr uint32_t redmax_off =
-      ored_in_ring ? kv_off + ST * kStageBytes : ored_off + kAttnComputeWarps * kMaxGroup * kHeadDim * 4;  // 4 x G
+  static constexpr uint32_t ored_off = kv_off;                                           // 4 x G x 128
+  static constexpr uint32_t redmax_off = kv_off + ST * kStageBytes;                      // 4 x G
   static constexpr uint32_t lred_off = redmax_off + kAttnComputeWarps * kMaxGroup * 4;  // 4 x G
   static constexpr uint32_t tab_off = lred_off + kAttnComputeWarps * kMaxGroup * 4;     // block-table window
   static constexpr uint32_t bar_off = tab_off + kTabWindow * 4;
@@ -80,8 +79,8 @@ struct AttnSmem {
   static constexpr uint32_t bytes = flag_off + 16 + 1024;
   static_assert(kAttnComputeWarps * kMaxGroup * kHeadDim * 4 <= ST * kStageBytes, "ored must fit in the ring");
 };
-// Two 3-stage CTAs (plus the 1 KB the SM reserves for each) share an SM's 228 KB.
-static_assert(2 * (AttnSmem<3>::bytes + 1024) <= 228 * 1024, "the 3-stage ring must let two CTAs share an SM");
+// Two CTAs (plus the 1 KB the SM reserves for each) share an SM's 228 KB.
+static_assert(2 * (AttnSmem<kAttnStages>::bytes + 1024) <= 228 * 1024, "the ring must let two CTAs share an SM");
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
                                             int c3, uint32_t bar, uint64_t policy) {
@@ -392,8 +391,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
   l += __shfl_xor_sync(0xffffffffu, l, 2);
   float *mred = redmax;                                  // [warp][G]
   float *lr = lred;                                      // [warp][G]
-  // When ored reuses the ring, every warp must be done reading its last chunk.
-  if constexpr (S::ored_in_ring) named_sync(1, kAttnComputeWarps * 32);
+  // ored reuses the ring: every warp must be done reading its last chunk.
+  named_sync(1, kAttnComputeWarps * 32);
   if (r < G) {
     if (cq == 0) {
       mred[warp * kMaxGroup + r] = m_run;
@@ -456,17 +455,6 @@ __global__ void __launch_bounds__(kHeadDim) attn_merge_kernel(const __grid_const
   out[d] = Elem<T>::from_float(den == 0.f ? 0.f : acc / den);
 }
 
-// Ring depth of the decode-attention kernel: 4 stages (one CTA per SM) by
-// default; DAK_B200_ATTN_STAGES=3 selects the 3-stage ring, with which two
-// CTAs share an SM.
-int attn_stages() {
-  static const int st = [] {
-    const char *v = getenv("DAK_B200_ATTN_STAGES");
-    return (v && v[0] == '3' && v[1] == 0) ? 3 : kAttnStages;
-  }();
-  return st;
-}
-
 template <typename T, int G, int ST>
 cudaError_t launch_g(const AttnParams &p, cudaStream_t stream) {
   auto kern = attn_decode_kernel<T, G, ST>;
@@ -481,12 +469,11 @@ cudaError_t launch_g(const AttnParams &p, cudaStream_t stream) {
 
 template <typename T>
 cudaError_t launch_t(const AttnParams &p, int group, cudaStream_t stream) {
-  const bool three = attn_stages() == 3;
   switch (group) {
-    case 1: return three ? launch_g<T, 1, 3>(p, stream) : launch_g<T, 1, kAttnStages>(p, stream);
-    case 2: return three ? launch_g<T, 2, 3>(p, stream) : launch_g<T, 2, kAttnStages>(p, stream);
-    case 4: return three ? launch_g<T, 4, 3>(p, stream) : launch_g<T, 4, kAttnStages>(p, stream);
-    case 8: return three ? launch_g<T, 8, 3>(p, stream) : launch_g<T, 8, kAttnStages>(p, stream);
+    case 1: return launch_g<T, 1, kAttnStages>(p, stream);
+    case 2: return launch_g<T, 2, kAttnStages>(p, stream);
+    case 4: return launch_g<T, 4, kAttnStages>(p, stream);
+    case 8: return launch_g<T, 8, kAttnStages>(p, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -26,21 +26,12 @@ int *device_status_word();
 // DAK_OK if `p` is memory of the current device or pinned host memory.
 int check_gpu_accessible(const void *p, const char *what);
 
-// Shared memory one linear-kernel CTA may fill with pipeline stages, in bytes.
-// All of it (227 KB) by default.  DAK_B200_SMEM_BUDGET_KB lowers it (not below
-// 64 KB) so that two CTAs fit on one SM: under programmatic dependent launch
-// the next layer's CTAs then stream their first weight stages while this
-// layer's last tiles finish.  A layout keeps at least two stages whatever the
-// budget, and the tcgen05 kernel only follows it while two CTAs' TMEM columns
-// fit in one SM.
-uint32_t linear_smem_budget();
-
 // Programmatic dependent launch of the decode-step kernels (RMSNorm, rotary,
-// SiLU-gate, KV append, decode attention and its merge): off unless
-// DAK_B200_PDL_DECODE=1, and never with DAK_B200_NO_PDL=1.  When on, each of
-// them is launched with programmatic stream serialization, waits for the
-// previous kernel (griddepcontrol.wait) before it touches memory, and lets the
-// next kernel be scheduled, so launches overlap the tail of the kernel before.
+// SiLU-gate, KV append, decode attention and its merge): on unless
+// DAK_B200_NO_PDL=1.  Each of them is launched with programmatic stream
+// serialization, waits for the previous kernel (griddepcontrol.wait) before it
+// touches memory, and lets the next kernel be scheduled, so launches overlap
+// the tail of the kernel before.
 bool decode_pdl_enabled();
 
 // cudaLaunchKernelEx with optional 1-D clusters (cluster > 1) and programmatic
@@ -96,9 +87,8 @@ cudaError_t launch_linear_mma(const LinearParams &p, int ntok_tmpl, int dtype, i
 size_t linear_wide_smem_bytes();
 int linear_wide_k_rows();
 cudaError_t launch_linear_wide(const LinearParams &p, int dtype, int grid, size_t smem, cudaStream_t stream);
-// Off unless DAK_B200_WIDE_PREFILL=1: batches above 256 tokens of a layer with
-// host-resident rows then go to the wide kernel in chunks of up to 512 tokens.
-bool wide_prefill_enabled();
+// Batches above 256 tokens of a layer with host-resident rows go to the wide
+// kernel in chunks of up to 512 tokens.
 
 // Sets, once per kernel and device, the kernel's dynamic shared-memory limit
 // to the device's opt-in maximum and allows non-portable cluster sizes.  Every

@@ -59,8 +59,7 @@ struct CoreLayout {
   }
   static int stages_for(int red_slots) {
     int s = kCoreStages;
-    const uint32_t budget = std::min(kCoreSmemBudget, linear_smem_budget());
-    while (s > 2 && CoreLayout(s).bytes(red_slots) > budget) --s;
+    while (s > 2 && CoreLayout(s).bytes(red_slots) > kCoreSmemBudget) --s;
     return s;
   }
 };

@@ -477,11 +477,8 @@ cudaError_t launch_dtype(const LinearParams &p, int ntokp, int grid, int cluster
 
 template <int NTOKP>
 int stages_for(int ks) {
-  // Two CTAs share an SM only if both TMEM allocations fit (512 columns).
-  const uint32_t budget =
-      2 * MmaLayout<NTOKP>::tmem_cols() <= 512 ? std::min(kSmemPerBlock, linear_smem_budget()) : kSmemPerBlock;
   int st = kMmaMaxStages;
-  while (st > 2 && MmaLayout<NTOKP>(st).bytes(ks) > budget) --st;
+  while (st > 2 && MmaLayout<NTOKP>(st).bytes(ks) > kSmemPerBlock) --st;
   return st;
 }
 

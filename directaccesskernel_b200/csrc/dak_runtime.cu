@@ -335,32 +335,10 @@ int desc_to_matrix(const void *blob, const char *what, MatView *out) {
 }
 }  // namespace
 
-uint32_t linear_smem_budget() {
-  static const uint32_t bytes = [] {
-    const uint32_t full = 227u * 1024u;
-    const char *v = getenv("DAK_B200_SMEM_BUDGET_KB");
-    if (!v || !v[0]) return full;
-    const long kb = strtol(v, nullptr, 10);
-    if (kb <= 0) return full;
-    return (uint32_t)std::min<long>(227, std::max<long>(64, kb)) * 1024u;
-  }();
-  return bytes;
-}
-
 bool decode_pdl_enabled() {
   static const bool on = [] {
     const char *off = getenv("DAK_B200_NO_PDL");
-    if (off && off[0] && off[0] != '0') return false;
-    const char *v = getenv("DAK_B200_PDL_DECODE");
-    return v && v[0] && v[0] != '0';
-  }();
-  return on;
-}
-
-bool wide_prefill_enabled() {
-  static const bool on = [] {
-    const char *v = getenv("DAK_B200_WIDE_PREFILL");
-    return v && v[0] && v[0] != '0';
+    return !(off && off[0] && off[0] != '0');
   }();
   return on;
 }
@@ -562,8 +540,9 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
   const int nkb = (int)((a->K + bk - 1) / bk);
 
   // Token chunks: the tcgen05 kernel serves up to 256 tokens per launch; the
-  // wide kernel, when enabled, up to 512 for a layer with host-resident rows.
-  const bool wide = mma && !ar && a->host_cols > 0 && a->ntok > kMmaMaxTok && wide_prefill_enabled();
+  // wide kernel up to 512 for a layer with host-resident rows, so that those
+  // rows cross the host link once per 512 tokens instead of once per 256.
+  const bool wide = mma && !ar && a->host_cols > 0 && a->ntok > kMmaMaxTok;
   const int64_t chunk = wide ? 2 * kMmaMaxTok : mma ? kMmaMaxTok : kCoreMaxTok;
   for (int64_t t0 = 0; t0 < a->ntok; t0 += chunk) {
     const int64_t nt = std::min(chunk, a->ntok - t0);
@@ -776,6 +755,24 @@ int gemv_from_descs(const void *a_h, const void *a_d, const void *b, const void 
     a.dev_ctas = d_M > 0 ? std::max(1, num_copy_blocks - hb) : 0;
     a.host_ksplit = std::max(1, h_spr);
     a.dev_ksplit = std::max(1, d_spr);
+  }
+  // The single-tier entry points (`gemv`, linearLayer.py:72-80 with the weight
+  // moved to "cpu") pass a pinned host weight as their only tier.  For batches
+  // above one tcgen05 launch, serve it as the host tier, so that it takes the
+  // kernel that streams host rows once for up to 512 tokens.
+  if (h_M == 0 && d_M > 0 && N > kMmaMaxTok) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, ad.base) == cudaSuccess && attr.type == cudaMemoryTypeHost) {
+      std::swap(a.w_host, a.w_dev);
+      std::swap(a.host_cols, a.dev_cols);
+      std::swap(a.ld_host, a.ld_dev);
+      a.host_col_offset = 0;
+      a.dev_col_offset = 0;
+      std::swap(a.host_ctas, a.dev_ctas);
+      std::swap(a.host_ksplit, a.dev_ksplit);
+    } else {
+      cudaGetLastError();
+    }
   }
   a.path = DAK_PATH_AUTO;
   return run_linear(&a, stream);

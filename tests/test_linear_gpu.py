@@ -5,7 +5,6 @@ Tolerance (from the task's parity bar): normwise max relative error
 max|y - y_ref| / max|y_ref| <= 1e-2 against FP32/FP64 accumulation; the
 kernels accumulate in FP32 and round once to 16 bits, so the observed error is
 about 1e-3."""
-import os
 
 import numpy as np
 import pytest
@@ -75,8 +74,6 @@ def test_tcgen05_path(shape, ntok):
         assert rel_err(y, ref) < TOL, (host_cols, rel_err(y, ref))
 
 
-@pytest.mark.skipif(os.environ.get("DAK_B200_WIDE_PREFILL") != "1",
-                    reason="the wide prefill kernel is opt-in: run with DAK_B200_WIDE_PREFILL=1")
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("ntok", [257, 300, 512, 700, 1024])
 @pytest.mark.parametrize("shape", [(256, 512), (384, 200), (1088, 4160)])
@@ -187,6 +184,26 @@ def test_single_tier_linear(device):
     lin.build_tma_desc()
     y = lin(x.cuda())
     assert rel_err(y.float().cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("ntok", [300, 512, 700])
+@pytest.mark.parametrize("blocks", [0, 64])
+def test_single_tier_host_weight_prefill(ntok, blocks):
+    """A whole weight in pinned host memory (linearLayer.py:72-80) at prefill
+    batch sizes: the single-tier entry point serves it as the host tier, on the
+    kernel that streams it once per 512 tokens; automatic and explicit plans."""
+    from directaccesskernel_b200.layers import Linear, LinearMulticast
+
+    w, x = _inputs(1024, 2048, ntok, seed=8)
+    ref = _oracle(w, x)
+    for cls in (Linear, LinearMulticast):
+        lin = _make_layer(cls, 1024, 2048, w)
+        lin.move_weight_to_device("cpu")
+        if blocks and cls is Linear:
+            lin.config(blocks, 2)
+        lin.build_tma_desc()
+        y = lin(x.cuda())
+        assert rel_err(y.float().cpu().numpy(), ref) < TOL, cls.__name__
 
 
 @pytest.mark.parametrize("prefill", [True, False])
