@@ -39,6 +39,11 @@ DEFAULT_HORIZONTAL_CONFIG = {
 # from the ratio and let the B200 schedule choose CTAs and split-K.
 B200_DEFAULT_SPLIT = (0, 0, 0, 0, 1, 1)
 
+# Split every horizontal module of a GPU gets when no per-shape table is used.
+# The GH200 and RTX6000 rows are the reference's built-in values
+# (placement.py:141-146); a caller's default_horizontal_config overrides them.
+_BUILTIN_SPLIT = {"GH200": (0, 0, 16, 112, 1, 1), "RTX6000": (0, 0, 8, 180, 1, 1), "B200": B200_DEFAULT_SPLIT}
+
 
 @dataclass(frozen=True)
 class ModelPlacementStats:
@@ -151,8 +156,8 @@ def _place_horizontal_linear(name, module, offload_ratio, *, gpu_name, use_confi
     """placement.py:99-130."""
     if not allow_edges and not 0.0 < offload_ratio < 1.0:
         raise ValueError(f"{name} is a horizontal Linear, so offload_ratio must be between 0 and 1; got {offload_ratio}")
-    h_m, d_m, h_blocks, d_blocks, h_sms_per_row, d_sms_per_row = _resolve_horizontal_split_config(
-        module, offload_ratio, gpu_name=gpu_name, use_config=use_config, horizontal_config=horizontal_config,
+    h_m, d_m, h_blocks, d_blocks, h_sms_per_row, d_sms_per_row = _split_plan(
+        module, gpu_name=gpu_name, use_config=use_config, horizontal_config=horizontal_config,
         default_horizontal_config=default_horizontal_config,
     )
     if allow_edges and h_m == 0 and d_m == 0:
@@ -165,61 +170,60 @@ def _place_horizontal_linear(name, module, offload_ratio, *, gpu_name, use_confi
                                    d_m, host_side=host_side)
 
 
-def _resolve_horizontal_split_config(module, offload_ratio, *, gpu_name, use_config, horizontal_config,
-                                     default_horizontal_config):
-    """placement.py:133-160, with B200 added to the built-in defaults."""
-    if default_horizontal_config is not None and gpu_name in default_horizontal_config:
-        config = default_horizontal_config[gpu_name]
-    elif gpu_name == "GH200":
-        config = (0, 0, 16, 112, 1, 1)
-    elif gpu_name == "RTX6000":
-        config = (0, 0, 8, 180, 1, 1)
-    elif gpu_name == "B200":
-        config = B200_DEFAULT_SPLIT
-    else:
+def _split_plan(module, *, gpu_name, use_config, horizontal_config, default_horizontal_config):
+    """The split tuple of one horizontal module (placement.py:133-160): the
+    GPU's default row, or with ``use_config`` the row of its weight shape in
+    ``horizontal_config[gpu_name]``.  A GPU with no default row raises
+    NotImplementedError, also when a shape table would be used; a missing table
+    or shape raises KeyError."""
+    defaults = dict(_BUILTIN_SPLIT)
+    defaults.update(default_horizontal_config or {})
+    if gpu_name not in defaults:
         raise NotImplementedError(f"GPU {gpu_name} not supported for horizontal split config")
     if not use_config:
-        return config
-    weight_shape = tuple(module.weight.shape)
-    gpu_config = horizontal_config.get(gpu_name)
-    if gpu_config is None:
+        return defaults[gpu_name]
+    table = horizontal_config.get(gpu_name)
+    if table is None:
         raise KeyError(f"Horizontal config for GPU {gpu_name} not found")
-    if weight_shape not in gpu_config:
-        raise KeyError(f"Weight shape {weight_shape} not found in horizontal config for {gpu_name}")
-    return gpu_config[weight_shape]
+    shape = tuple(module.weight.shape)
+    if shape not in table:
+        raise KeyError(f"Weight shape {shape} not found in horizontal config for {gpu_name}")
+    return table[shape]
 
 
-def _move_non_custom_direct_tensors(module, custom_types, device) -> None:
-    """placement.py:163-172."""
-    if isinstance(module, custom_types):
+def _move_param(param, device) -> None:
+    """Moves a parameter's data (and gradient) to ``device`` in place, keeping
+    the Parameter object that modules and optimizers hold."""
+    if param is None:
         return
-    _move_direct_parameters_and_buffers(module, device)
-    for child in module.children():
-        _move_non_custom_direct_tensors(child, custom_types, device)
+    param.data = param.data.to(device, non_blocking=True)
+    if param.grad is not None:
+        param.grad.data = param.grad.data.to(device, non_blocking=True)
 
 
-def _move_direct_parameters_and_buffers(module: nn.Module, device) -> None:
-    """placement.py:175-187."""
+def _move_non_custom_direct_tensors(model: nn.Module, custom_types, device) -> None:
+    """Every parameter and buffer of ``model`` outside the replaced linears goes
+    to ``device`` (placement.py:163-187); the replaced linears' weights are
+    placed by their splits.  Walks the module tree without recursion."""
+    pending = [model]
     with torch.no_grad():
-        for param in module._parameters.values():
-            if param is not None:
-                param.data = param.data.to(device, non_blocking=True)
-                if param.grad is not None:
-                    param.grad.data = param.grad.data.to(device, non_blocking=True)
-        for name, buffer in module._buffers.items():
-            if buffer is not None:
-                module._buffers[name] = buffer.to(device, non_blocking=True)
+        while pending:
+            module = pending.pop()
+            if isinstance(module, custom_types):
+                continue
+            for param in module._parameters.values():
+                _move_param(param, device)
+            for key, buf in list(module._buffers.items()):
+                if buf is not None:
+                    module._buffers[key] = buf.to(device, non_blocking=True)
+            pending.extend(module.children())
 
 
 def _move_custom_linear_bias(module: nn.Module, device) -> None:
-    """placement.py:190-197."""
-    bias = getattr(module, "bias", None)
-    if bias is None:
-        return
+    """A replaced linear's bias lives with the rest of the model on ``device``
+    (placement.py:190-197); its weight stays where the split put it."""
     with torch.no_grad():
-        bias.data = bias.data.to(device, non_blocking=True)
-        if bias.grad is not None:
-            bias.grad.data = bias.grad.data.to(device, non_blocking=True)
+        _move_param(getattr(module, "bias", None), device)
 
 
 def _custom_linear_types() -> tuple[type[nn.Module], ...]:

@@ -259,3 +259,31 @@ def test_nvtx_tracing_is_opt_in():
         out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, cwd=REPO)
         assert out.returncode == 0, out.stderr
         assert out.stdout.strip() == want
+
+
+@pytest.mark.parametrize("family", ["opt", "llama"])
+def test_replacement_config_round_trips_every_stored_field(family):
+    """Every field the reference stores on a Hugging Face config
+    (linear_replacement.py:42-75) comes back unchanged; absent attributes read
+    as the reference's defaults."""
+    from directaccesskernel_b200 import linear_replacement as lr
+
+    cfg = lr.LinearReplacementConfig("horizontal", smem_size=65536, num_copy_blocks=32, device="cuda:1",
+                                     dtype=torch.bfloat16, multicast_kernel=True, drop_bias=False, skip_init=False)
+    conf = types.SimpleNamespace()
+    getattr(lr, f"set_{family}_linear_config")(conf, cfg)
+    assert all(k.startswith(f"{family}_linear_") for k in vars(conf))
+    assert getattr(lr, f"get_{family}_linear_config")(conf) == cfg
+    empty = getattr(lr, f"get_{family}_linear_config")(types.SimpleNamespace())
+    assert empty == lr.LinearReplacementConfig("vanila")
+    # A bare linear type stands for its default configuration.
+    getattr(lr, f"set_{family}_linear_config")(conf, "host")
+    assert getattr(lr, f"get_{family}_linear_config")(conf) == lr.LinearReplacementConfig("host")
+
+
+def test_replacement_of_a_missing_linear_raises():
+    from directaccesskernel_b200 import linear_replacement as lr
+
+    model = _tiny_opt(9)
+    with pytest.raises(AttributeError):
+        lr.replace_opt_linears(model, lr.LinearReplacementConfig("vanila", device="cpu"), ["q_proj", "no_such"])
