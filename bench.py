@@ -16,8 +16,10 @@ Metric: effective weight GB/s (weight bytes / time, benchmark_linear.py:341),
 with a roofline of max((1-r) W / HBM, r W / host link) per layer.
 
 Usage (driver contract): python bench.py [--gpus N] [--steps K] [--warmup W]
-[--impl reference]; under torchrun one process per GPU, weak scaling (every
-rank streams its own copy of the sweep over its own host link).
+[--impl reference]; under torchrun one process per GPU.  The linear workloads
+then run tensor-parallel (strong scaling): every layer is column-parallel, each
+GPU streams its shard of the weights from its own HBM and over its own host
+link, and NCCL all-gathers y after every layer.
 """
 from __future__ import annotations
 
@@ -43,14 +45,17 @@ FALLBACK_TFLOPS = 1590.0
 FALLBACK_TFLOPS_SUSTAINED = 1400.0
 # Tokens per launch of the tcgen05 linear kernel; larger batches run in chunks.
 MMA_MAX_TOKENS = 256
+# Peer copy bandwidth per direction per GPU over NVLink 5 measured on this
+# pool's B200 boxes (900 GB/s nominal): the roofline term of the all-gather.
+NVLINK_GBS = 770.0
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch divided by
-# the launch's device-tier bytes ((1 - r) W + x + y), from full-size ncu captures
-# of the Llama-3-8B layers at r = 0 and 0.5 (profiles/linear_core_llama8b_m1.md,
-# profiles/linear_mma_llama8b_m16.md): 1.000-1.004, mean 1.002.  The host tier's
-# bytes cross PCIe and never touch DRAM.
+# the launch's device-tier bytes ((1 - r) W + x + y), measured with ncu on
+# full-size launches of both linear kernels on the Llama-3-8B layers at r = 0
+# and 0.5: 1.000-1.004, mean 1.002.  The host tier's bytes cross PCIe and never
+# touch DRAM.
 DRAM_PER_DEVICE_BYTE = 1.002
-# Same for the attention kernel (profiles/attn_decode_config3.md): 541.6 MB of
-# DRAM traffic for 536.9 MB of device-resident K/V.
+# Same for the decode-attention kernel on BASELINE config 3 (one full-size
+# launch): 541.6 MB of DRAM traffic for 536.9 MB of device-resident K/V.
 ATTN_DRAM_PER_DEVICE_BYTE = 1.0088
 
 
@@ -229,16 +234,37 @@ def layer_roofline(m: int, n: int, k: int, host_bytes: int, hbm_gbs: float, host
     return which, terms[which]
 
 
-def build_layers(torch, tokens, ratios, seed=0):
-    """One module per (shape, ratio), placed as placement.py places it."""
+def build_layers(torch, tokens, ratios, seed=0, rank=0, world=1, host_frac=None, keep_weights=False):
+    """One module per (shape, ratio), placed as placement.py places it.
+
+    With ``world`` > 1 every layer is column-parallel (tensor parallel): every
+    rank generates the same full weight, keeps output features [rank N/G,
+    (rank+1) N/G) as an offloaded module split between its own HBM and its own
+    pinned host memory, and all-gathers y after each call.  ``host_frac[r]`` is
+    this rank's host fraction for sweep ratio r (the mean over ranks is r)."""
     from directaccesskernel_b200.layers import Linear, LinearHorizontal
     from directaccesskernel_b200.utils import get_smem_size, split_horizontal
 
     g = torch.Generator(device="cuda").manual_seed(seed)
-    layers = []
+    layers, weights = [], {}
     for name, (n, k) in LLAMA8B.items():
         w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).half()
+        if keep_weights:
+            weights[name] = w.cpu()
         for r in ratios:
+            if world > 1:
+                from directaccesskernel_b200.tp import ColumnParallelLinear, make_offloaded_shard, shard_rows
+
+                rr = host_frac[r] if host_frac else r
+                local = make_offloaded_shard(shard_rows(w, rank, world), rr)
+                if isinstance(local, LinearHorizontal):
+                    host_rows = local.out_features_h
+                else:
+                    host_rows = n // world if local.weight.device.type == "cpu" else 0
+                lin = ColumnParallelLinear(local, n)
+                layers.append({"name": name, "n": n, "k": k, "ratio": r, "rank_ratio": rr, "mod": lin,
+                               "w_bytes": n * k * 2, "rank_n": n // world, "host_bytes": host_rows * k * 2})
+                continue
             if 0.0 < r < 1.0:
                 lin = LinearHorizontal(k, n, get_smem_size(), 0, device="cuda", dtype=torch.float16, skip_init=True)
                 with torch.no_grad():
@@ -254,36 +280,105 @@ def build_layers(torch, tokens, ratios, seed=0):
                 lin.move_weight_to_device("cpu" if r >= 1.0 else "cuda")
                 lin.build_tma_desc()
                 host_bytes = n * k * 2 if r >= 1.0 else 0
-            layers.append({"name": name, "n": n, "k": k, "ratio": r, "mod": lin, "w_bytes": n * k * 2,
-                           "host_bytes": host_bytes})
+            layers.append({"name": name, "n": n, "k": k, "ratio": r, "rank_ratio": r, "mod": lin, "w_bytes": n * k * 2,
+                           "rank_n": n, "host_bytes": host_bytes})
         del w
     torch.cuda.synchronize()
-    return layers
+    return (layers, weights) if keep_weights else layers
+
+
+def linear_sweep(args):
+    """(prefill, tokens, ratios) of the linear workloads."""
+    prefill = args.workload == "prefill"
+    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else ([512] if prefill else list(TOKENS))
+    ratios = ([float(r) for r in args.ratios.split(",")] if args.ratios
+              else ([0.0, 0.5, 1.0] if prefill else list(RATIOS)))
+    return prefill, tokens, ratios
+
+
+def linear_metric_config(prefill, tokens, ratios, world):
+    """Metric name and `config` of the linear workloads, the same for both arms."""
+    if prefill:
+        metric = f"offloaded linear effective weight GB/s (Llama-3-8B layers, prefill M={tokens})"
+        workload = (f"large-N prefill: Llama-3-8B qkv/o/gate_up/down x M{tokens} x r{ratios}; up to 512 tokens "
+                    f"per launch for layers with host rows, {MMA_MAX_TOKENS} otherwise")
+    else:
+        metric = "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)"
+        workload = "BASELINE config 2: Llama-3-8B qkv/o/gate_up/down x M{1,4,16,64} x r{0,.25,.5,.75,1}"
+    calls = len(tokens) * len(ratios) * len(LLAMA8B)
+    config = {"workload": workload,
+              "tokens": tokens, "ratios": ratios, "layers_per_step": calls,
+              "weight_bytes_per_step": len(tokens) * len(ratios) * sum(2 * n * k for (n, k) in LLAMA8B.values()),
+              "host_rows": "first (reference split_horizontal)",
+              "l2": "no flush: 436 MB of weights per (M, r) pass exceed the 126 MB L2",
+              "timing": f"device: one CUDA graph per step ({calls} launches) replayed K times; "
+                        "per-launch breakdown: per-layer graphs back to back with events between",
+              "parallelism": "single GPU (tp1)"}
+    if world > 1:
+        config["parallelism"] = (f"tp{world}: every layer column-parallel (output features sharded over {world} "
+                                 "GPUs, each shard split between its own HBM and its own pinned host memory), "
+                                 "y all-gathered over NCCL after each layer; the whole job streams each weight once")
+    return metric, config
+
+
+def linear_parity(torch, layers, calls, outputs, weights, x_dev, tol=1e-2):
+    """Max relative error (max|y - ref| / max|ref|) of every call's output against
+    the reference's own CPU computation of the layer, torch F.linear in FP32 on
+    the host cores (benchmark_linear.py:121-123: nn.Linear on float copies)."""
+    import torch.nn.functional as F
+
+    worst, refs = 0.0, {}
+    for (l, m), y in zip(calls, outputs):
+        key = (l["name"], m)
+        if key not in refs:
+            x = x_dev[(m, l["k"])].reshape(m, l["k"]).float().cpu()
+            refs[key] = F.linear(x, weights[l["name"]].float())
+        ref = refs[key]
+        err = ((y.reshape(m, -1).float().cpu() - ref).abs().max() / ref.abs().max()).item()
+        worst = max(worst, err)
+    return {"max_rel_err": round(worst, 6), "cases": len(calls), "tolerance": tol, "ok": worst <= tol,
+            "reference": "torch F.linear(x.float(), W.float()) on the host cores (benchmark_linear.py:121-123)",
+            "checked": "rank 0, on the full (all-gathered) outputs of every layer call"}
 
 
 def run_linear(args, torch, rank, world):
     from directaccesskernel_b200 import runtime
 
-    prefill = args.workload == "prefill"
-    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else ([512] if prefill else list(TOKENS))
-    ratios = ([float(r) for r in args.ratios.split(",")] if args.ratios
-              else ([0.0, 0.5, 1.0] if prefill else list(RATIOS)))
+    prefill, tokens, ratios = linear_sweep(args)
+    tp = world > 1
     hbm_gbs, peak_kind = measured_peaks()
     tflops, tflops_kind = measured_tensor_tflops()
     dma_gbs, tma_host_gbs = host_link_probe(torch, runtime, world)
     host_gbs = max(dma_gbs, tma_host_gbs)
     hbm_read_gbs = hbm_read_probe(torch, runtime)
 
-    layers = build_layers(torch, tokens, ratios, seed=rank)
-    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    host_frac, host_by_rank = None, [host_gbs]
+    if tp:
+        # Each rank streams its own shard over its own host link; all links are
+        # measured at once.  Host rows go to the ranks in proportion to their
+        # concurrent GPU-initiated read bandwidth, so that all host streams end
+        # together; the mean host fraction per layer stays the sweep's ratio.
+        bw = torch.tensor([tma_host_gbs, host_gbs], dtype=torch.float64, device="cuda")
+        parts = [torch.zeros_like(bw) for _ in range(world)]
+        torch.distributed.all_gather(parts, bw)
+        tma_by_rank = [float(t[0]) for t in parts]
+        host_by_rank = [float(t[1]) for t in parts]
+        host_frac = {r: (r if (args.no_balance or r in (0.0, 1.0)) else balanced_host_fractions(r, tma_by_rank)[rank])
+                     for r in ratios}
+
+    built = build_layers(torch, tokens, ratios, seed=0 if tp else rank, rank=rank, world=world,
+                         host_frac=host_frac, keep_weights=(rank == 0))
+    layers, weights = built if rank == 0 else (built, None)
+    gen = torch.Generator(device="cuda").manual_seed(1234 if tp else 1234 + rank)
     x_dev = {(m, k): torch.randn(m, 1, k, generator=gen, device="cuda").half()
-             for m in tokens for k in {l["k"] for l in layers}}
+             for m in tokens for k in sorted({l["k"] for l in layers})}
     calls = [(l, m) for m in tokens for l in layers]
 
     # The device-timed region replays CUDA graphs, as the reference's decode
     # loop does (benchmark_opt.py:344-357): one graph per step for `value`,
     # and one graph per layer call, replayed back to back with events between
-    # them, for the per-launch roofline breakdown.
+    # them, for the per-launch roofline breakdown.  Under tensor parallelism
+    # each call's all-gather (NCCL) is captured in the same graphs.
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -359,12 +454,16 @@ def run_linear(args, torch, rank, world):
     status = runtime.device_status()
     if status != 0:
         raise RuntimeError(f"device error word {status} after the timed region")
+    # Graphs that hold NCCL calls are released before the process group goes.
+    g = None
+    del g, step_graph, call_graphs, ratio_graphs
+    torch.cuda.synchronize()
 
     # ---- end to end through the module API with host buffers (e2e)
     x_host = {key: v.cpu().pin_memory() for key, v in x_dev.items()}
     y_host = [torch.empty(m, 1, l["n"], dtype=torch.float16).pin_memory() for (l, m) in calls]
-    h2d = sum(x_host[(m, l["k"])].numel() * 2 for (l, m) in calls)
-    d2h = sum(y.numel() * 2 for y in y_host)
+    h2d = world * sum(x_host[(m, l["k"])].numel() * 2 for (l, m) in calls)
+    d2h = world * sum(y.numel() * 2 for y in y_host)
 
     def step_e2e():
         for i, (l, m) in enumerate(calls):
@@ -385,6 +484,13 @@ def run_linear(args, torch, rank, world):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
+    # ---- parity of the outputs of one eager pass (all ranks take part in the
+    # all-gathers; rank 0 checks the gathered outputs on the host)
+    outputs = [l["mod"](x_dev[(m, l["k"])]).clone() for (l, m) in calls]
+    torch.cuda.synchronize()
+    parity = linear_parity(torch, layers, calls, outputs, weights, x_dev) if rank == 0 else None
+    del outputs
+
     # ---- reduce over ranks (max time, summed bytes)
     w_bytes_step = sum(l["w_bytes"] for (l, m) in calls)
     kernel_ms = sum(launch_ms)
@@ -393,20 +499,33 @@ def run_linear(args, torch, rank, world):
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
     total_ms, kernel_ms, e2e_ms = times.tolist()
 
-    # Roofline per layer call: max((1-r) W / HBM, r W / host, 2 M N K / tensor peak);
-    # x and y bytes ride with HBM.  The compute term only binds for prefill-sized
-    # M (at M = 64 it is a quarter of the HBM term).
+    # Roofline per layer call: max((1-r)W/HBM, rW/host, 2MNK/tensor peak), with
+    # x and y bytes riding with HBM; the compute term only binds for
+    # prefill-sized M.  Under tensor parallelism each rank's term uses its own
+    # shard, host rows and concurrently measured host link, plus the bytes the
+    # all-gather brings in over NVLink; a call is bound by its slowest rank.
+    per_call = []
+    for (l, m) in calls:
+        which, t_s = layer_roofline(m, l["rank_n"], l["k"], l["host_bytes"], hbm_gbs, host_gbs, tflops)
+        if tp:
+            t_nv = (world - 1) / world * m * l["n"] * 2 / (NVLINK_GBS * 1e9)
+            if t_nv > t_s:
+                which, t_s = "nvlink", t_nv
+        per_call.append((which, t_s * 1e3))
+    roof_t = torch.tensor([t for (_, t) in per_call], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(roof_t, op=torch.distributed.ReduceOp.MAX)
+    roof_call = roof_t.tolist()
     roof_ms = 0.0
     alg_bytes = 0
     dram_bytes = 0.0
     per_ratio = {}
-    bound_ms = {"hbm": 0.0, "host": 0.0, "tensor": 0.0}
+    bound_ms = {"hbm": 0.0, "host": 0.0, "tensor": 0.0, "nvlink": 0.0}
     for i, (l, m) in enumerate(calls):
         io = (m * l["k"] + m * l["n"]) * 2
-        dram_bytes += (l["w_bytes"] - l["host_bytes"] + io) * DRAM_PER_DEVICE_BYTE
-        which, t_roof_s = layer_roofline(m, l["n"], l["k"], l["host_bytes"], hbm_gbs, host_gbs, tflops)
-        t_roof = t_roof_s * 1e3
-        bound_ms[which] += t_roof * args.steps
+        dram_bytes += (l["rank_n"] * l["k"] * 2 - l["host_bytes"] + io) * DRAM_PER_DEVICE_BYTE
+        t_roof = roof_call[i]
+        bound_ms[per_call[i][0]] += t_roof * args.steps
         roof_ms += t_roof * args.steps
         alg_bytes += l["w_bytes"] + io
         pr = per_ratio.setdefault(l["ratio"], {"bytes": 0, "ms": ratio_ms[l["ratio"]], "roof_ms": 0.0,
@@ -414,51 +533,47 @@ def run_linear(args, torch, rank, world):
         pr["bytes"] += l["w_bytes"] * args.steps
         pr["isolated_ms"] += launch_ms[i]
         pr["roof_ms"] += t_roof * args.steps
-    # Achieved bandwidth of the dominant kernel family averaged over the timed
-    # launches of the step graph (total algorithmic bytes / device time).
+    # Achieved bandwidth averaged over the timed launches of the step graph
+    # (total algorithmic bytes of the job / device time).
     achieved = alg_bytes * args.steps / (total_ms * 1e-3) / 1e9
     peak_eff = alg_bytes * args.steps / (roof_ms * 1e-3) / 1e9
-    value = world * w_bytes_step * args.steps / (total_ms * 1e-3) / 1e9
-    e2e = world * w_bytes_step * args.steps / (e2e_ms * 1e-3) / 1e9
+    value = w_bytes_step * args.steps / (total_ms * 1e-3) / 1e9
+    e2e = w_bytes_step * args.steps / (e2e_ms * 1e-3) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_linear(tokens)
+        cpu = cpu_baseline_linear(tokens, ratios)
 
-    details = [{"layer": l["name"], "m": m, "ratio": l["ratio"], "ms": launch_ms[i] / args.steps,
-                "gbs": l["w_bytes"] / (launch_ms[i] / args.steps * 1e-3) / 1e9}
+    details = [{"layer": l["name"], "m": m, "ratio": l["ratio"], "rank_ratio": l["rank_ratio"],
+                "ms": launch_ms[i] / args.steps, "gbs": l["w_bytes"] / (launch_ms[i] / args.steps * 1e-3) / 1e9}
                for i, (l, m) in enumerate(calls)]
     if args.details and rank == 0:
         Path(args.details).write_text(json.dumps(details, indent=1))
-    if prefill:
-        metric = f"offloaded linear effective weight GB/s (Llama-3-8B layers, prefill M={tokens})"
-        workload = (f"large-N prefill: Llama-3-8B qkv/o/gate_up/down x M{tokens} x r{ratios}; the tcgen05 kernel "
-                    f"takes {MMA_MAX_TOKENS} tokens per launch")
-    else:
-        metric = "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)"
-        workload = "BASELINE config 2: Llama-3-8B qkv/o/gate_up/down x M{1,4,16,64} x r{0,.25,.5,.75,1}"
+    metric, config = linear_metric_config(prefill, tokens, ratios, world)
+    tp_info = None
+    if tp:
+        tp_info = {"host_fraction_per_rank": {str(r): round(f, 4) for r, f in host_frac.items()},
+                   "host_fraction_basis": "rank 0's share; shares are proportional to each rank's concurrent "
+                                          "GPU-initiated host read bandwidth, mean over ranks = r",
+                   "host_link_gbs_per_rank": [round(v, 2) for v in host_by_rank]}
     line = {
         "metric": metric,
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong" if tp else "weak",
         "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic N(0,0.02) weights, N(0,1) activations",
-        "config": {"workload": workload,
-                   "tokens": tokens, "ratios": ratios, "layers_per_step": len(calls),
-                   "weight_bytes_per_step": w_bytes_step, "host_rows": "first (reference split_horizontal)",
-                   "l2": "no flush: 436 MB of weights per (M, r) pass exceed the 126 MB L2",
-                   "timing": "device: one CUDA graph per step (80 launches) replayed K times; "
-                             "per-launch breakdown: per-layer graphs back to back with events between",
-                   "parallelism": f"replicas x{world} (weak, no collective)"},
+        "config": config,
         "roofline": {"bound": "tensor" if bound_ms["tensor"] > bound_ms["hbm"] + bound_ms["host"] else "hbm",
                      "achieved": round(achieved, 2), "peak": round(peak_eff, 2), "unit": "GB/s",
                      "frac": round(achieved / peak_eff, 4),
                      "traffic": round(dram_bytes / len(calls)),
-                     "traffic_basis": "DRAM bytes per launch, step average: ncu dram read+write = "
+                     "traffic_basis": "DRAM bytes per launch on rank 0, step average: ncu dram read+write = "
                                       f"{DRAM_PER_DEVICE_BYTE} x device-tier bytes on full-size captures; the "
                                       "host tier's bytes cross PCIe, so traffic < algorithmic bytes "
                                       f"({round(alg_bytes / len(calls))} per launch)",
-                     "peak_model": "combined HBM + host-link (+ tensor) roofline, sum over layers of "
-                                   "max((1-r)W/HBM, rW/host, 2MNK/tensor peak)",
+                     "peak_model": "combined HBM + host-link (+ tensor, + NVLink all-gather under tp) roofline, sum "
+                                   "over layers of the slowest rank's max((1-r)W/HBM, rW/host, 2MNK/tensor peak, "
+                                   "gathered bytes/NVLink)",
                      "bound_ms_by_term": {k: round(v, 4) for k, v in bound_ms.items()},
                      "tensor_tflops": tflops, "tensor_peak_kind": tflops_kind,
                      "hbm_gbs": hbm_gbs, "hbm_peak_kind": peak_kind, "host_link_gbs": round(host_gbs, 2),
@@ -471,46 +586,100 @@ def run_linear(args, torch, rank, world):
                      "timing": "achieved = algorithmic bytes / device time of the step graph; per_ratio from one "
                                "graph per ratio; isolated_launch_frac from single-launch graphs with events between"},
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": sum(-(-m // MMA_MAX_TOKENS) for (l, m) in calls) * args.steps,
+        "gpu_launches": world * sum(-(-m // (2 * MMA_MAX_TOKENS if l["host_bytes"] and m > MMA_MAX_TOKENS
+                                             else MMA_MAX_TOKENS)) for (l, m) in calls) * args.steps,
         "clocks": clock,
+        "parity": parity,
     }
+    if tp:
+        line["tp"] = tp_info
+        line["roofline"]["nvlink_gbs"] = NVLINK_GBS
+        line["roofline"]["host_link_basis"] = "each rank's own link, all ranks streaming at once"
     if cpu is not None:
         line["cpu_baseline"] = cpu
     return line
 
 
-_CPU_WEIGHTS: dict = {}
+class CpuLinearSweep:
+    """The sweep's layer calls computed on the host cores, for the CPU baseline
+    and the reference arm.  ``impl`` "torch" is the reference's own computation
+    of a layer, torch F.linear on FP32 copies (benchmark_linear.py:121-123 runs
+    nn.Linear); "port" is the oracle's numpy restatement.  Weights and inputs
+    are built once, before anything is timed.  One pass computes every layer
+    call of one step (shapes x M x ratios; the host computation does not depend
+    on the offload ratio), and only whole passes are timed."""
 
+    def __init__(self, tokens, ratios, impl: str = "torch", seed: int = 0):
+        import numpy as np
 
-def cpu_baseline_linear(tokens, budget_s: float = 20.0):
-    """The oracle port (numpy FP32 x @ W^T, all host threads) on a bounded sample
-    of the sweep: every shape at every M once, weights resident in FP32.  CPU time
-    does not depend on the offload ratio.  Reported in the same unit (fp16 weight
-    bytes / time)."""
-    import numpy as np
+        self.impl, self.tokens, self.ratios = impl, list(tokens), list(ratios)
+        self.threads = os.cpu_count()
+        rng = np.random.default_rng(seed)
+        self.w, self.x = {}, {}
+        for name, (n, k) in LLAMA8B.items():
+            w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+            for m in self.tokens:
+                self.x[(name, m)] = rng.standard_normal((m, k), dtype=np.float32)
+            self.w[name] = w
+        if impl == "torch":
+            import torch
 
-    import oracle  # noqa: F401  (the checker; timed here as the CPU baseline)
+            torch.set_num_threads(self.threads)
+            self.w = {k: torch.from_numpy(v) for k, v in self.w.items()}
+            self.x = {k: torch.from_numpy(v) for k, v in self.x.items()}
+        self.bytes_per_pass = len(self.ratios) * len(self.tokens) * sum(2 * n * k for (n, k) in LLAMA8B.values())
+        self.calls_per_pass = len(self.ratios) * len(self.tokens) * len(LLAMA8B)
 
-    rng = np.random.default_rng(0)
-    t_total, bytes_total = 0.0, 0
-    start = time.perf_counter()
-    for name, (n, k) in LLAMA8B.items():
-        if name not in _CPU_WEIGHTS:
-            _CPU_WEIGHTS[name] = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
-        w = _CPU_WEIGHTS[name]
-        for m in tokens:
-            x = rng.standard_normal((m, k), dtype=np.float32)
+    def one_pass(self):
+        if self.impl == "torch":
+            import torch.nn.functional as F
+
+            for _ in self.ratios:
+                for m in self.tokens:
+                    for name in LLAMA8B:
+                        F.linear(self.x[(name, m)], self.w[name])
+        else:
+            import numpy as np
+
+            import oracle  # the checker, timed here as the CPU baseline
+
+            for _ in self.ratios:
+                for m in self.tokens:
+                    for name in LLAMA8B:
+                        oracle.linear(self.x[(name, m)], self.w[name], acc=np.float32)
+
+    def timed_passes(self, passes: int, warmup: int = 1) -> list[float]:
+        for _ in range(warmup):
+            self.one_pass()
+        times = []
+        for _ in range(passes):
             t = time.perf_counter()
-            y = oracle.linear(x, w, acc=np.float32)
-            t_total += time.perf_counter() - t
-            bytes_total += n * k * 2
-            del y
-        if time.perf_counter() - start > budget_s:
-            break
-    cores = os.cpu_count()
-    return {"value": round(bytes_total / t_total / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"numpy FP32 x@W^T over the 4 Llama-3-8B shapes x M{list(tokens)} once each "
-                      f"(CPU time is independent of the offload ratio), {cores} threads"}
+            self.one_pass()
+            times.append(time.perf_counter() - t)
+        return times
+
+    def sample(self) -> str:
+        what = ("torch F.linear(x, W) on FP32 copies (the reference's computation, benchmark_linear.py:121-123)"
+                if self.impl == "torch" else "the oracle's numpy FP32 x @ W^T")
+        return (f"{what}: whole passes over the {self.calls_per_pass} layer calls of one step "
+                f"(4 Llama-3-8B shapes x M{self.tokens} x {len(self.ratios)} ratios; host time does not depend on "
+                f"the ratio), weights built before timing, {self.threads} threads; GB/s of fp16 weight bytes")
+
+
+def cpu_baseline_linear(tokens, ratios, passes: int = 3):
+    """cpu_baseline of the GPU arm: the median of whole timed passes of the
+    reference's computation (torch F.linear, FP32) on all host cores, with the
+    oracle port's figure beside it."""
+    out = {}
+    for impl in ("torch", "port"):
+        sweep = CpuLinearSweep(tokens, ratios, impl)
+        times = sweep.timed_passes(passes)
+        out[impl] = (sweep.bytes_per_pass / statistics.median(times) / 1e9, sweep, len(times))
+        del sweep
+    v, sweep, n = out["torch"]
+    return {"value": round(v, 3), "unit": "GB/s", "cores": sweep.threads, "kind": "reference",
+            "sample": sweep.sample() + f"; median of {n} passes",
+            "port_value": round(out["port"][0], 3), "port_kind": "port (numpy oracle, same passes)"}
 
 
 def run_attention(args, torch, rank, world):
@@ -597,7 +766,8 @@ def run_attention(args, torch, rank, world):
                      "peak": round(kv_bytes / (roof_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                      "frac": round(roof_ms * args.steps / ms, 4),
                      "traffic": round((kv_bytes - host_bytes) * ATTN_DRAM_PER_DEVICE_BYTE),
-                     "traffic_basis": "ncu dram read+write of one full-size launch (profiles/attn_decode_config3.md)",
+                     "traffic_basis": "ncu dram read+write of one full-size config-3 launch: 541.6 MB for 536.9 MB "
+                                      "of device-resident K/V",
                      "peak_model": "max(device KV / HBM, host KV / host link)", "hbm_gbs": hbm_gbs,
                      "hbm_peak_kind": peak_kind, "host_link_gbs": round(host_gbs, 2)},
         "e2e": {"value": round(world * kv_bytes * args.steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -1006,28 +1176,31 @@ def run_reference(args):
             "cpu_baseline": cpu,
             "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
-    prefill = args.workload == "prefill"
-    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else ([512] if prefill else list(TOKENS))
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_baseline_linear(tokens[:1], budget_s=5.0)
-    vals = []
+    prefill, tokens, ratios = linear_sweep(args)
+    metric, config = linear_metric_config(prefill, tokens, ratios, args.gpus)
+    sweep = CpuLinearSweep(tokens, ratios, "torch")
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        vals.append(cpu_baseline_linear(tokens, budget_s=20.0)["value"])
+    times = sweep.timed_passes(args.steps, warmup=args.warmup)
     elapsed = time.perf_counter() - t0
-    v = statistics.median(vals)
-    cpu = cpu_baseline_linear(tokens[:1], budget_s=2.0)
-    cpu["value"] = v
+    v = round(sweep.bytes_per_pass * len(times) / sum(times) / 1e9, 3)
+    sample, threads = sweep.sample(), sweep.threads
+    del sweep
+    port = CpuLinearSweep(tokens, ratios, "port")
+    pt = port.timed_passes(max(1, min(args.steps, 3)), warmup=1)
+    port_v = round(port.bytes_per_pass * len(pt) / sum(pt) / 1e9, 3)
+    del port
     return {
-        "metric": (f"offloaded linear effective weight GB/s (Llama-3-8B layers, prefill M={tokens})" if prefill
-                   else "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)"), "impl": "reference",
+        "metric": metric, "impl": "reference",
         "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(elapsed / max(1, args.steps) * 1e3, 2), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": ("large-N prefill" if prefill else "BASELINE config 2") + " sample on host cores",
-                   "tokens": tokens},
-        "cpu_baseline": {**cpu, "kind": "port"},
+        "ms_per_step": round(sum(times) / len(times) * 1e3, 2), "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 else "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic N(0,0.02) weights, N(0,1) activations",
+        "config": config,
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "reference",
+                         "sample": sample + f"; {len(times)} timed steps, one pass per step",
+                         "port_value": port_v, "port_kind": "port (numpy oracle, same passes)"},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(elapsed, 2),
     }
 
 
@@ -1047,7 +1220,17 @@ def main():
     if world > 1:
         from datetime import timedelta
 
+        # NCCL reports each communicator's set-up (rank, nranks, Init COMPLETE)
+        # on stderr, unless the caller chose its own NCCL logging.
+        if "NCCL_DEBUG" not in os.environ:
+            os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE="/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        probe = torch.ones(1, device="cuda")
+        torch.distributed.all_reduce(probe)
+        torch.cuda.synchronize()
+        print(f"[bench] rank {rank}: NCCL {'.'.join(map(str, torch.cuda.nccl.version()))} communicator up, "
+              f"nranks={torch.distributed.get_world_size()}, all-reduce check {int(probe.item())} == {world}",
+              file=sys.stderr, flush=True)
     try:
         fn = {"attention": run_attention, "opt66b": run_opt66b, "llama70b": run_llama70b}.get(args.workload, run_linear)
         line = fn(args, torch, rank, world)

@@ -390,7 +390,7 @@ MAKERS = ["split_tables", "desc_args", "linear_split", "placement", "linear_ref"
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--ref", default="/root/reference", help="checkout of shouxulin/DirectAccessKernel")
+    ap.add_argument("--ref", required=True, help="checkout of shouxulin/DirectAccessKernel")
     ap.add_argument("--out", default=str(HERE))
     ap.add_argument("--only", nargs="*", choices=MAKERS, help="regenerate only these fixtures")
     args = ap.parse_args()
