@@ -65,7 +65,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["linear", "prefill", "attention", "opt66b", "llama70b"], default="linear",
+    ap.add_argument("--workload", choices=["linear", "prefill", "attention", "opt66b", "llama70b", "plan-sweep"],
+                    default="linear",
                     help="prefill: the Llama-3-8B layers at 512 tokens, r in {0, 0.5, 1} (large-N path)")
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
     ap.add_argument("--batch", type=int, default=32, help="llama70b: sequences")
@@ -598,6 +599,82 @@ def run_linear(args, torch, rank, world):
     if cpu is not None:
         line["cpu_baseline"] = cpu
     return line
+
+
+def run_plan_sweep(args, torch, rank, world):
+    """Launch-plan sweep of the HBM-only (r = 0) Llama-3-8B layers, one GPU: the
+    automatic plan and explicit (dev_ctas, dev_ksplit) plans, each timed two
+    ways.  Chained: a CUDA graph of 8 calls on distinct weight copies (more than
+    L2), so the overlap of consecutive launches counts; per call = graph / 8.
+    Isolated: a graph of one call.  One JSON record per plan goes to
+    ``--details``; the line summarises the automatic plan against the best."""
+    from directaccesskernel_b200 import runtime
+
+    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else list(TOKENS)
+    copies, reps = 8, max(3, args.steps)
+    stream = torch.cuda.current_stream()
+
+    def timed(graph):
+        for _ in range(max(1, args.warmup)):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    records = []
+    for name, (n, k) in LLAMA8B.items():
+        ws = [(torch.randn(k, n, device="cuda") * 0.02).half() for _ in range(copies)]
+        for m in tokens:
+            x = torch.randn(m, k, device="cuda").half()
+            ys = [torch.empty(m, n, device="cuda", dtype=torch.float16) for _ in range(copies)]
+            kss = (1, 2, 4) if m > 2 else (1, 2, 4, 8)
+            plans = [(0, 0)] + [(c, ks) for ks in kss for c in (32, 48, 64, 96, 128, 144, 148)
+                                if 1 <= c // ks <= (n + 63) // 64]
+            for (c, ks) in plans:
+                def call(i):
+                    runtime.linear_split(x, ys[i], None, ws[i], dev_ctas=c, dev_ksplit=ks)
+
+                for i in range(copies):
+                    call(i)
+                side = torch.cuda.Stream()
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    chain, one = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(chain):
+                        for i in range(copies):
+                            call(i)
+                    with torch.cuda.graph(one):
+                        call(0)
+                stream.wait_stream(side)
+                chained, isolated = timed(chain) / copies, timed(one)
+                del chain, one
+                records.append({"shape": name, "m": m, "ctas": c, "ksplit": ks, "chained_us": round(chained * 1e3, 3),
+                                "isolated_us": round(isolated * 1e3, 3),
+                                "chained_tbs": round(2 * n * k / (chained * 1e-3) / 1e12, 3)})
+        del ws
+        torch.cuda.empty_cache()
+    if runtime.device_status() != 0:
+        raise RuntimeError("device error word set during the plan sweep")
+    if args.details:
+        Path(args.details).write_text("\n".join(json.dumps(r) for r in records) + "\n")
+    auto = {(r["shape"], r["m"]): r["chained_us"] for r in records if r["ctas"] == 0}
+    best = {}
+    for r in records:
+        key = (r["shape"], r["m"])
+        best[key] = min(best.get(key, float("inf")), r["chained_us"])
+    hbm_gbs, peak_kind = measured_peaks()
+    roof_us = sum(2 * n * k / (hbm_gbs * 1e9) * 1e6 for (n, k) in LLAMA8B.values()) * len(tokens)
+    return {"metric": "HBM-only linear launch plans: chained microseconds per call, automatic vs best explicit plan",
+            "value": round(sum(auto.values()), 2), "unit": "us (sum over shapes x M, automatic plan)", "n_gpus": 1,
+            "steps": reps, "warmup": args.warmup, "higher_is_better": False,
+            "best_explicit_us": round(sum(best.values()), 2), "hbm_roofline_us": round(roof_us, 2),
+            "hbm_gbs": hbm_gbs, "hbm_peak_kind": peak_kind, "plans": len(records),
+            "config": {"workload": f"Llama-3-8B qkv/o/gate_up/down in HBM x M{tokens}; {copies} weight copies per "
+                                   "chain (more than L2)"}}
 
 
 class CpuLinearSweep:
@@ -1232,7 +1309,8 @@ def main():
               f"nranks={torch.distributed.get_world_size()}, all-reduce check {int(probe.item())} == {world}",
               file=sys.stderr, flush=True)
     try:
-        fn = {"attention": run_attention, "opt66b": run_opt66b, "llama70b": run_llama70b}.get(args.workload, run_linear)
+        fn = {"attention": run_attention, "opt66b": run_opt66b, "llama70b": run_llama70b,
+              "plan-sweep": run_plan_sweep}.get(args.workload, run_linear)
         line = fn(args, torch, rank, world)
         if rank == 0:
             print(json.dumps(line), flush=True)

@@ -94,10 +94,16 @@ def make_offloaded_shard(weight_shard: torch.Tensor, offload_ratio: float, *, ho
     """An offloaded module holding ``weight_shard`` ([N_r, K_r]): LinearHorizontal
     for 0 < r < 1, a single-tier Linear in HBM (r = 0) or pinned host memory (r = 1)."""
     from .layers import Linear, LinearHorizontal
-    from .utils import get_smem_size
+    from .utils import get_smem_size, split_horizontal
 
     n, k = weight_shard.shape
     dt = weight_shard.dtype if weight_shard.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    if 0.0 < offload_ratio < 1.0:
+        # A small shard may round to no host rows, or to all of them (rows move
+        # in 64-row boxes): it is then a single-tier module.
+        h_m, d_m = split_horizontal((n, k), offload_ratio)
+        if h_m == 0 or d_m == 0:
+            offload_ratio = 1.0 if h_m else 0.0
     if 0.0 < offload_ratio < 1.0:
         mod = LinearHorizontal(k, n, get_smem_size(), 0, device=device, dtype=dt, skip_init=True)
         with torch.no_grad():
