@@ -103,6 +103,23 @@ __device__ __forceinline__ void cluster_sync_all() {
   cluster_arrive();
   cluster_wait();
 }
+// Arrival without release semantics: the thread's earlier writes are not made
+// visible to the cluster first, so it does not wait for outstanding global
+// stores (which the end of the kernel orders anyway).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+// Last barrier of a cluster before its CTAs exit: no CTA leaves while a peer
+// may still write to its shared memory.  Threads whose last act was a write to
+// a peer's shared memory (`remote`) arrive with release semantics, so that
+// write lands before the peer can leave; the others arrive relaxed.
+__device__ __forceinline__ void cluster_exit_sync(bool remote) {
+  if (remote)
+    cluster_arrive();
+  else
+    cluster_arrive_relaxed();
+  cluster_wait();
+}
 
 // Named barrier over `count` threads (warp multiples), id 1..15.
 __device__ __forceinline__ void named_sync(int id, int count) {

@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
   // until this grid has completed.
   if (threadIdx.x == 0) griddep_launch_dependents();
 
+  bool sent_remote = false;  // this thread's last tile ended with writes to a peer's shared memory
   if (warp == kCoreConsumerWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && ntiles > 0 && kb1 > kb0) {
@@ -277,6 +278,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
               st_cluster_v4(dst + 16, out[4], out[5], out[6], out[7]);
             }
             mbar_arrive_remote(mapa_shared(red_full, leader));
+            sent_remote = true;
             write_out = false;
           } else {
             // Leader: add the members' partials once all of them have landed.
@@ -291,7 +293,9 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
               }
             }
             __syncwarp();
-            if (lane == 0)
+            // Members wait for this before sending their next partial; after
+            // the last tile there is none, and a member may already have left.
+            if (lane == 0 && j + 1 < ntiles)
               for (int m = 1; m < ks; ++m) mbar_arrive_remote(mapa_shared(red_free, my_rank + m));
           }
           ++nred;
@@ -317,8 +321,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1)
       }
     }
   }
-  // No CTA leaves while a peer may still touch its shared memory.
-  cluster_sync_all();
+  // No CTA leaves while a peer may still touch its shared memory.  Members'
+  // last partials were waited for by their leaders, and leaders send no
+  // release after the last tile, so only the members' own remote writes need
+  // release semantics; the output stores need none.
+  cluster_exit_sync(sent_remote);
 }
 
 template <typename T>

@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   // until this grid has completed.
   if (threadIdx.x == 0) griddep_launch_dependents();
 
+  bool sent_remote = false;  // this thread's last tile ended with writes to a peer's shared memory
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && ntiles > 0 && kb1 > kb0) {
@@ -325,7 +326,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           }
           if (ks > 1) {
             __syncwarp();
-            if (lane == 0)
+            // Senders wait for this before sending their next partial; after
+            // the last tile there is none, and a sender may already have left.
+            if (lane == 0 && j + 1 < ntiles)
               for (int m = 0; m < ks; ++m)
                 if (m != r) mbar_arrive_remote(mapa_shared(red_free, my_rank - r + m));
           }
@@ -346,6 +349,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               st_cluster_v4(dst_base + (uint32_t)(c0 + j) * 4, v[j], v[j + 1], v[j + 2], v[j + 3]);
           }
           mbar_arrive_remote(mapa_shared(red_full, owner_rank));
+          sent_remote = true;
         }
         if (ks > 1) ++nred;
         tc_fence_before();
@@ -447,8 +451,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
   }
 
+  // No CTA leaves while a peer may still touch its shared memory (see
+  // cluster_exit_sync): owners waited for every partial sent to them and send
+  // no release after the last tile, so only senders need release semantics;
+  // the output stores need none.
   tc_fence_before();
-  cluster_sync_all();
+  cluster_exit_sync(sent_remote);
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, L.tmem_cols());
 }
