@@ -64,6 +64,113 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const void *x, co
   }
 }
 
+// Vectorized RMSNorm for rows whose buffers are 16-byte aligned and whose
+// length is a multiple of 8: one CTA per row, each thread owning NV 16-byte
+// vectors (8 elements each) of it.  Every thread issues all its loads (x,
+// residual, weight) before using any, so a row costs one memory round trip
+// instead of one per 256 elements; h stays in registers between the sum of
+// squares and the output.  Same arithmetic as rmsnorm_kernel: h = x (+
+// residual, rounded to 16 bit), statistics in FP32, out = w * round16(h * inv).
+template <typename T, int NV>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(const void *x, const void *res, const void *w,
+                                                                   void *out, void *res_out, int cols, long long ld,
+                                                                   float eps, int pdl) {
+  pdl_enter(pdl);
+  const long long row = blockIdx.x;
+  const int nvec = cols / 8;
+  const uint4 *xr = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + row * ld);
+  const uint4 *rr = res ? reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(res) + row * ld) : nullptr;
+  const uint4 *wv = reinterpret_cast<const uint4 *>(w);
+  uint4 hv[NV], wr[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = threadIdx.x + j * kNormThreads;
+    hv[j] = v < nvec ? xr[v] : make_uint4(0u, 0u, 0u, 0u);
+    wr[j] = v < nvec ? wv[v] : make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (rr) {
+    uint4 rv[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = threadIdx.x + j * kNormThreads;
+      rv[j] = v < nvec ? rr[v] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      uint32_t *h = reinterpret_cast<uint32_t *>(&hv[j]);
+      const uint32_t *r = reinterpret_cast<const uint32_t *>(&rv[j]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = Elem<T>::to_float2(h[e]), b = Elem<T>::to_float2(r[e]);
+        h[e] = Elem<T>::pack2(a.x + b.x, a.y + b.y);  // rounded to 16 bit, as torch's add
+      }
+    }
+    uint4 *ro = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(res_out) + row * ld);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = threadIdx.x + j * kNormThreads;
+      if (v < nvec) ro[v] = hv[j];
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t *h = reinterpret_cast<const uint32_t *>(&hv[j]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = Elem<T>::to_float2(h[e]);
+      ss = fmaf(a.x, a.x, ss);
+      ss = fmaf(a.y, a.y, ss);
+    }
+  }
+  __shared__ float red[kNormThreads / 32];
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / (float)cols + eps);
+  uint4 *orow = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + row * (long long)cols);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = threadIdx.x + j * kNormThreads;
+    if (v >= nvec) continue;
+    uint4 o;
+    const uint32_t *h = reinterpret_cast<const uint32_t *>(&hv[j]);
+    const uint32_t *wk = reinterpret_cast<const uint32_t *>(&wr[j]);
+    uint32_t *ov = reinterpret_cast<uint32_t *>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = Elem<T>::to_float2(h[e]), ww = Elem<T>::to_float2(wk[e]);
+      const float n0 = Elem<T>::to_float(Elem<T>::from_float(a.x * inv));
+      const float n1 = Elem<T>::to_float(Elem<T>::from_float(a.y * inv));
+      ov[e] = Elem<T>::pack2(ww.x * n0, ww.y * n1);
+    }
+    orow[v] = o;
+  }
+}
+
+template <typename T>
+cudaError_t launch_rmsnorm(cudaStream_t s, int rows, int cols, int pdl, const void *x, const void *res,
+                           const void *w, void *out, void *res_out, long long ld, float eps) {
+  const dim3 grid(rows), block(kNormThreads);
+  const int nvec = cols / 8;
+  const bool vec = cols % 8 == 0 && ld % 8 == 0 && nvec <= 8 * kNormThreads &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(res) |
+                     reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out) |
+                     reinterpret_cast<uintptr_t>(res_out)) & 15u) == 0;
+  if (!vec) return launch_ex(rmsnorm_kernel<T>, grid, block, 0, s, 1, pdl, x, res, w, out, res_out, cols, ld, eps, pdl);
+  if (nvec <= kNormThreads)
+    return launch_ex(rmsnorm_vec_kernel<T, 1>, grid, block, 0, s, 1, pdl, x, res, w, out, res_out, cols, ld, eps, pdl);
+  if (nvec <= 2 * kNormThreads)
+    return launch_ex(rmsnorm_vec_kernel<T, 2>, grid, block, 0, s, 1, pdl, x, res, w, out, res_out, cols, ld, eps, pdl);
+  if (nvec <= 4 * kNormThreads)
+    return launch_ex(rmsnorm_vec_kernel<T, 4>, grid, block, 0, s, 1, pdl, x, res, w, out, res_out, cols, ld, eps, pdl);
+  return launch_ex(rmsnorm_vec_kernel<T, 8>, grid, block, 0, s, 1, pdl, x, res, w, out, res_out, cols, ld, eps, pdl);
+}
+
 // One CTA per (sequence, head) of q, k and v, head_dim / 2 threads: for q and k,
 // thread i rotates the pair (i, i + d/2) with cos/sin of position * inv_freq[i]
 // rounded to 16 bit (transformers apply_rotary_pos_emb, default rotary
@@ -86,12 +193,8 @@ __global__ void rope_qk_kernel(const void *qkv, long long ld, const int32_t *pos
     vo[i + half] = in[src + i + half];
     return;
   }
-  const float f = (float)pos[b] * inv_freq[i];
-  const float c = r16<T>(cosf(f)), s = r16<T>(sinf(f));
-  const float x1 = ld1<T>(qkv, src + i), x2 = ld1<T>(qkv, src + i + half);
-  // out[i] = x1*c + (-x2)*s ; out[i + d/2] = x2*c + x1*s, each product and sum rounded.
-  const float o1 = r16<T>(r16<T>(x1 * c) + r16<T>(-x2 * s));
-  const float o2 = r16<T>(r16<T>(x2 * c) + r16<T>(x1 * s));
+  float o1, o2;
+  rope_pair<T>(ld1<T>(qkv, src + i), ld1<T>(qkv, src + i + half), (float)pos[b] * inv_freq[i], o1, o2);
   void *dst;
   long long off;
   if (hh < q_heads) {
@@ -248,10 +351,9 @@ extern "C" int dak_rmsnorm(const void *x, const void *residual, const void *weig
   const int pdl = decode_pdl_enabled() ? 1 : 0;
   const cudaError_t e =
       dtype == DAK_DTYPE_F16
-          ? launch_ex(rmsnorm_kernel<__half>, dim3(rows), dim3(kNormThreads), 0, s, 1, pdl, x, residual, weight, out,
-                      residual_out, cols, (long long)ld, eps, pdl)
-          : launch_ex(rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), 0, s, 1, pdl, x, residual, weight,
-                      out, residual_out, cols, (long long)ld, eps, pdl);
+          ? launch_rmsnorm<__half>(s, rows, cols, pdl, x, residual, weight, out, residual_out, (long long)ld, eps)
+          : launch_rmsnorm<__nv_bfloat16>(s, rows, cols, pdl, x, residual, weight, out, residual_out, (long long)ld,
+                                          eps);
   return cuda_status(e, "rmsnorm launch");
 }
 
