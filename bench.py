@@ -38,6 +38,8 @@ if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
 LLAMA8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 4096), "down": (4096, 14336)}
+# One tensor-parallel rank's layers of the Llama-3-70B decoder at TP 8 (config 5).
+LLAMA70B_TP8 = {"qkv": (1280, 8192), "o": (8192, 1024), "gate_up": (7168, 8192), "down": (8192, 3584)}
 TOKENS = (1, 4, 16, 64)
 RATIOS = (0.0, 0.25, 0.5, 0.75, 1.0)
 FALLBACK_HBM_GBS = 6650.0
@@ -90,6 +92,8 @@ def parse_args():
     ap.add_argument("--ratios", type=str, default=None, help="comma list overriding the ratio sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--details", type=str, default=None, help="write per-layer results (JSON) here")
+    ap.add_argument("--sweep-shapes", choices=["llama8b", "llama70b-tp8"], default="llama8b",
+                    help="plan-sweep: the Llama-3-8B layers, or one TP8 rank's Llama-3-70B layers")
     return ap.parse_args()
 
 
@@ -610,7 +614,9 @@ def run_plan_sweep(args, torch, rank, world):
     ``--details``; the line summarises the automatic plan against the best."""
     from directaccesskernel_b200 import runtime
 
-    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else list(TOKENS)
+    tp8 = args.sweep_shapes == "llama70b-tp8"
+    shapes = LLAMA70B_TP8 if tp8 else LLAMA8B
+    tokens = [int(t) for t in args.tokens.split(",")] if args.tokens else ([32] if tp8 else list(TOKENS))
     copies, reps = 8, max(3, args.steps)
     stream = torch.cuda.current_stream()
 
@@ -626,7 +632,7 @@ def run_plan_sweep(args, torch, rank, world):
         return e0.elapsed_time(e1) / reps
 
     records = []
-    for name, (n, k) in LLAMA8B.items():
+    for name, (n, k) in shapes.items():
         ws = [(torch.randn(k, n, device="cuda") * 0.02).half() for _ in range(copies)]
         for m in tokens:
             x = torch.randn(m, k, device="cuda").half()
@@ -667,14 +673,14 @@ def run_plan_sweep(args, torch, rank, world):
         key = (r["shape"], r["m"])
         best[key] = min(best.get(key, float("inf")), r["chained_us"])
     hbm_gbs, peak_kind = measured_peaks()
-    roof_us = sum(2 * n * k / (hbm_gbs * 1e9) * 1e6 for (n, k) in LLAMA8B.values()) * len(tokens)
+    roof_us = sum(2 * n * k / (hbm_gbs * 1e9) * 1e6 for (n, k) in shapes.values()) * len(tokens)
     return {"metric": "HBM-only linear launch plans: chained microseconds per call, automatic vs best explicit plan",
             "value": round(sum(auto.values()), 2), "unit": "us (sum over shapes x M, automatic plan)", "n_gpus": 1,
             "steps": reps, "warmup": args.warmup, "higher_is_better": False,
             "best_explicit_us": round(sum(best.values()), 2), "hbm_roofline_us": round(roof_us, 2),
             "hbm_gbs": hbm_gbs, "hbm_peak_kind": peak_kind, "plans": len(records),
-            "config": {"workload": f"Llama-3-8B qkv/o/gate_up/down in HBM x M{tokens}; {copies} weight copies per "
-                                   "chain (more than L2)"}}
+            "config": {"workload": (f"{'one TP8 rank of Llama-3-70B' if tp8 else 'Llama-3-8B'} qkv/o/gate_up/down in "
+                                    f"HBM x M{tokens}; {copies} weight copies per chain (more than L2)")}}
 
 
 class CpuLinearSweep:

@@ -283,27 +283,17 @@ def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_de
 
 
 @traced
-def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.Tensor | None,
-                    v_pool_dev: torch.Tensor | None, k_pool_host: torch.Tensor | None,
-                    v_pool_host: torch.Tensor | None, block_table: torch.Tensor, positions: torch.Tensor) -> None:
-    """Writes k_new/v_new [B, Hkv, D] of one new token per sequence into the paged
-    pools (the layout of ``decode_paged``) at ``positions`` [B] (int32, CUDA): device
-    pages in HBM, host pages straight into pinned host memory from the GPU.
-    Replaces the reference's per-step host-cache update
-    (app/python/pinned_static_cache.py:47-107)."""
-    if k_new.shape != v_new.shape or k_new.dim() != 3 or k_new.stride(2) != 1 or v_new.stride() != k_new.stride():
-        raise RuntimeError("k_new and v_new must be [B, Hkv, D] with equal strides and a contiguous last dimension")
-    if k_new.dtype not in (torch.float16, torch.bfloat16) or v_new.dtype != k_new.dtype:
-        raise RuntimeError("k_new and v_new must be float16 or bfloat16")
+def _kv_append_args(B: int, Hkv: int, D: int, dtype: torch.dtype, k_pool_dev, v_pool_dev, k_pool_host, v_pool_host,
+                    block_table: torch.Tensor, positions: torch.Tensor):
+    """Checked KvAppendArgs for the paged pools (the layout of ``decode_paged``)."""
     pool = k_pool_dev if k_pool_dev is not None else k_pool_host
     if pool is None:
         raise RuntimeError("no KV pool given")
-    B, Hkv, D = k_new.shape
     for t, nm, on_dev in ((k_pool_dev, "k_pool_dev", True), (v_pool_dev, "v_pool_dev", True),
                           (k_pool_host, "k_pool_host", False), (v_pool_host, "v_pool_host", False)):
         if t is None:
             continue
-        if t.dim() != 4 or t.size(1) != Hkv or t.size(3) != D or not t.is_contiguous() or t.dtype != k_new.dtype:
+        if t.dim() != 4 or t.size(1) != Hkv or t.size(3) != D or not t.is_contiguous() or t.dtype != dtype:
             raise RuntimeError(f"{nm} must be a contiguous [pages, {Hkv}, page_size, {D}] tensor of the KV dtype")
         if t.size(2) != pool.size(2):
             raise RuntimeError("all pools must share page_size")
@@ -316,8 +306,6 @@ def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.
     if positions.dtype != torch.int32 or not positions.is_cuda or positions.numel() != B or not positions.is_contiguous():
         raise RuntimeError("positions must be a contiguous int32 CUDA tensor [B]")
     a = _lib.KvAppendArgs()
-    a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
-    a.new_batch_stride, a.new_head_stride = k_new.stride(0), k_new.stride(1)
     if k_pool_dev is not None:
         a.k_pool_dev, a.v_pool_dev, a.dev_pages = k_pool_dev.data_ptr(), v_pool_dev.data_ptr(), k_pool_dev.size(0)
     if k_pool_host is not None:
@@ -325,8 +313,49 @@ def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.
     a.block_table, a.table_stride, a.max_pages = block_table.data_ptr(), block_table.stride(0), block_table.size(1)
     a.positions = positions.data_ptr()
     a.batch, a.kv_heads, a.head_dim, a.page_size = B, Hkv, D, pool.size(2)
-    a.dtype = dak_dtype(k_new.dtype)
+    a.dtype = dak_dtype(dtype)
+    return a
+
+
+def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.Tensor | None,
+                    v_pool_dev: torch.Tensor | None, k_pool_host: torch.Tensor | None,
+                    v_pool_host: torch.Tensor | None, block_table: torch.Tensor, positions: torch.Tensor) -> None:
+    """Writes k_new/v_new [B, Hkv, D] of one new token per sequence into the paged
+    pools (the layout of ``decode_paged``) at ``positions`` [B] (int32, CUDA): device
+    pages in HBM, host pages straight into pinned host memory from the GPU.
+    Replaces the reference's per-step host-cache update
+    (app/python/pinned_static_cache.py:47-107)."""
+    if k_new.shape != v_new.shape or k_new.dim() != 3 or k_new.stride(2) != 1 or v_new.stride() != k_new.stride():
+        raise RuntimeError("k_new and v_new must be [B, Hkv, D] with equal strides and a contiguous last dimension")
+    if k_new.dtype not in (torch.float16, torch.bfloat16) or v_new.dtype != k_new.dtype:
+        raise RuntimeError("k_new and v_new must be float16 or bfloat16")
+    B, Hkv, D = k_new.shape
+    a = _kv_append_args(B, Hkv, D, k_new.dtype, k_pool_dev, v_pool_dev, k_pool_host, v_pool_host, block_table,
+                        positions)
+    a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
+    a.new_batch_stride, a.new_head_stride = k_new.stride(0), k_new.stride(1)
     check(LIB.dak_kv_append_paged(ctypes.byref(a), _stream_ptr()), "kv_append_paged")
+
+
+def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, q_heads: int, kv_heads: int,
+                   head_dim: int, q_out: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_dev: torch.Tensor | None,
+                   k_pool_host: torch.Tensor | None, v_pool_host: torch.Tensor | None,
+                   block_table: torch.Tensor) -> None:
+    """One decode step's rotary embedding and KV append in one launch: the q heads
+    of ``qkv`` [B, (q_heads + 2 kv_heads) * head_dim] rotated into ``q_out``
+    [B, q_heads, head_dim]; the rotated k heads and the v heads written into
+    the paged pools at ``positions``, exactly as ``decode_ops.rope_qk`` followed by
+    ``kv_append_paged`` would write them."""
+    if qkv.dim() != 2 or qkv.stride(1) != 1 or qkv.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("qkv must be a 16-bit [B, (q_heads + 2 kv_heads) * head_dim] tensor, last dim contiguous")
+    if not q_out.is_contiguous() or q_out.dtype != qkv.dtype or q_out.numel() != qkv.shape[0] * q_heads * head_dim:
+        raise RuntimeError("q_out must be a contiguous [B, q_heads, head_dim] tensor of the qkv dtype")
+    if inv_freq.dtype != torch.float32 or not inv_freq.is_cuda or inv_freq.numel() != head_dim // 2:
+        raise RuntimeError("inv_freq must be a float32 CUDA tensor of head_dim / 2 entries")
+    a = _kv_append_args(qkv.shape[0], kv_heads, head_dim, qkv.dtype, k_pool_dev, v_pool_dev, k_pool_host,
+                        v_pool_host, block_table, positions)
+    check(LIB.dak_rope_kv_append(qkv.data_ptr(), qkv.stride(0), inv_freq.data_ptr(), q_out.data_ptr(), q_heads,
+                                 ctypes.byref(a), _stream_ptr()), "rope_kv_append")
 
 
 # ------------------------------------------------------------ Hugging Face hook

@@ -69,6 +69,18 @@ template <> struct Elem<__nv_bfloat16> {
   }
 };
 
+// Rotary embedding of the pair (x1, x2) = (x[i], x[i + d/2]) by the angle
+// position * inv_freq[i], with cos, sin, every product and every sum rounded to
+// the 16-bit type, as transformers' apply_rotary_pos_emb computes it on 16-bit
+// tensors: o1 = x1 c + (-x2) s, o2 = x2 c + x1 s.
+template <typename T>
+__device__ __forceinline__ void rope_pair(float x1, float x2, float angle, float &o1, float &o2) {
+  auto r16 = [](float v) { return Elem<T>::to_float(Elem<T>::from_float(v)); };
+  const float c = r16(cosf(angle)), s = r16(sinf(angle));
+  o1 = r16(r16(x1 * c) + r16(-x2 * s));
+  o2 = r16(r16(x2 * c) + r16(x1 * s));
+}
+
 // ---------------------------------------------------------------- addresses
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

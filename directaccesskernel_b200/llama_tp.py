@@ -12,9 +12,9 @@ B200s.  Each rank holds 1/G of every layer Megatron-style:
 Every linear is an offloaded module (``layers.LinearHorizontal``): its host rows
 sit in pinned memory and stream over this GPU's own host link.  The KV cache is
 paged (64-token pages): the first pages of every sequence live in pinned host
-memory, the rest in HBM; ``attention.kv_append_paged`` writes each new token
-straight into its page and ``attention.decode_paged`` reads both tiers in one
-launch.  A decode step, greedy pick included, is one CUDA graph.
+memory, the rest in HBM; ``attention.rope_kv_append`` rotates each new token's
+k and writes it with v straight into its page, and ``attention.decode_paged``
+reads both tiers in one launch.  A decode step, greedy pick included, is one CUDA graph.
 
 The layer arithmetic follows transformers' Llama (RMSNorm in FP32, rotary
 embedding in the activation dtype, SiLU-gated MLP), which is also what the
@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
-from .attention import auto_split_size, decode_paged, kv_append_paged
+from .attention import auto_split_size, decode_paged, rope_kv_append
 
 # Tokens per KV page.  One page of one KV head is a TMA box of page x 64 dims per
 # half head; 64-token pages give 8 KB boxes, which stream from HBM about twice
@@ -277,8 +277,6 @@ class TPLlamaDecoder(nn.Module):
         self.hidden = torch.empty(B, h, dtype=self.dtype, device=self.device)  # running residual stream
         self.x_buf = torch.empty(B, h, dtype=self.dtype, device=self.device)
         self.q_buf = torch.empty(B, self.hq, d, dtype=self.dtype, device=self.device)
-        self.k_buf = torch.empty(B, self.hkv, d, dtype=self.dtype, device=self.device)
-        self.v_buf = torch.empty(B, self.hkv, d, dtype=self.dtype, device=self.device)
         self.act_buf = torch.empty(B, self.ffn_r, dtype=self.dtype, device=self.device)
         self.o_buf = torch.empty(B, h, dtype=self.dtype, device=self.device)
         self.dn_buf = torch.empty(B, h, dtype=self.dtype, device=self.device)
@@ -318,9 +316,10 @@ class TPLlamaDecoder(nn.Module):
     def forward_step(self, keep_logits: bool = False) -> torch.Tensor:
         """One decode step on the static buffers: embeds ``ids`` at ``pos``, writes
         their K/V, and leaves the greedy tokens in ``next_ids``; advances nothing.
-        Per layer: RMSNorm (residual add fused), qkv, rotary, KV append, attention,
-        o + all-reduce, RMSNorm, gate_up, SiLU-gate, down + all-reduce."""
-        from .decode_ops import rmsnorm, rope_qk, silu_mul
+        Per layer: RMSNorm (residual add fused), qkv, rotary and KV append (one
+        kernel), attention, o + all-reduce, RMSNorm, gate_up, SiLU-gate, down +
+        all-reduce."""
+        from .decode_ops import rmsnorm, silu_mul
 
         s, B, d = self.s, self.B, self.s.head_dim
         t = self._span
@@ -334,11 +333,10 @@ class TPLlamaDecoder(nn.Module):
         for l, layer in enumerate(self.layers):
             with t("qkv"):
                 qkv = layer.qkv(x)
-            with t("rope"):
-                rope_qk(qkv, self.pos, self.inv_freq, self.hq, self.hkv, d, self.q_buf, self.k_buf, self.v_buf)
             kdev, vdev, khost, vhost = self._pools(l)
-            with t("kv_append"):
-                kv_append_paged(self.k_buf, self.v_buf, kdev, vdev, khost, vhost, self.block_table, self.pos)
+            with t("rope+kv_append"):
+                rope_kv_append(qkv, self.pos, self.inv_freq, self.hq, self.hkv, d, self.q_buf, kdev, vdev, khost,
+                               vhost, self.block_table)
             with t("attention"):
                 decode_paged(self.q_buf, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale,
                              self.split, out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
@@ -416,12 +414,12 @@ class TPLlamaDecoder(nn.Module):
 
     def kernel_launches_per_step(self) -> int:
         """Launches of this library's kernels in one ``forward_step``: the first
-        RMSNorm; per layer the four linears, rotary, KV append, attention (plus the
-        split merge when a sequence spans several splits), SiLU-gate and two
-        RMSNorms; then lm_head.  The torch ops around them (embedding gather,
+        RMSNorm; per layer the four linears, rotary with the KV append, attention
+        (plus the split merge when a sequence spans several splits), SiLU-gate and
+        two RMSNorms; then lm_head.  The torch ops around them (embedding gather,
         greedy pick) and NCCL's kernels are not counted."""
         merge = 1 if -(-self.max_ctx // self.split) > 1 else 0
-        return 1 + len(self.layers) * (10 + merge) + 1
+        return 1 + len(self.layers) * (9 + merge) + 1
 
     def advance(self) -> None:
         """Feeds the greedy tokens back and moves every sequence one position on."""

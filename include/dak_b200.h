@@ -337,6 +337,19 @@ typedef struct dak_kv_append_args {
 } dak_kv_append_args;
 DAK_API int dak_kv_append_paged(const dak_kv_append_args *args, void *stream);
 
+/* Rotary embedding and KV append of one decode step in one launch: for a
+ * fused projection qkv [batch, (q_heads + 2 kv_heads) * head_dim] (row stride
+ * ld), the q heads are rotated into q_out [batch, q_heads, head_dim] and the k
+ * heads (rotated) and v heads are written into the paged pools exactly as
+ * dak_rope_qk followed by dak_kv_append_paged would write them, positions and
+ * pools taken from `kv` (kv->k_new / v_new are not read).  inv_freq holds
+ * head_dim / 2 FP32 frequencies.  Out-of-range table entries are recorded in
+ * the device error word and skipped.  No reference counterpart: the reference
+ * applies rotary in torch (vanila_llama.py:212-246) and copies new K/V to its
+ * host cache on the CPU (pinned_static_cache.py:47-107). */
+DAK_API int dak_rope_kv_append(const void *qkv, int64_t ld, const float *inv_freq, void *q_out, int q_heads,
+                               const dak_kv_append_args *kv, void *stream);
+
 /* --------------------------------------------------- decode-layer helpers */
 /* The element-wise steps of a Llama decode layer around the linears and the
  * attention.  No reference counterpart as kernels: the reference runs them as

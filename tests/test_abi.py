@@ -190,6 +190,25 @@ def test_allreduce_and_kv_append_argument_checks():
     assert _status(L.dak_kv_append_paged, ctypes.byref(a), None)[0] == _lib.DAK_ERR_UNSUPPORTED
 
 
+def test_rope_kv_append_argument_checks():
+    """The fused rotary + KV append shares the append's pool checks (k_new / v_new
+    are not required) and checks its own qkv arguments, before any launch."""
+    from directaccesskernel_b200 import _lib
+
+    L = _lib.LIB
+    buf = 0x10000
+    a = _lib.KvAppendArgs()
+    a.batch, a.kv_heads, a.head_dim, a.page_size, a.max_pages, a.dtype = 2, 1, 128, 16, 4, _lib.DTYPE_F16
+    st, msg = _status(L.dak_rope_kv_append, buf, 1280, buf, buf, 8, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "block_table and positions" in msg
+    a.block_table = a.positions = buf
+    a.table_stride = 4
+    st, msg = _status(L.dak_rope_kv_append, buf, 1280, buf, buf, 8, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "no KV pool" in msg
+    st, msg = _status(L.dak_rope_kv_append, buf, 1280, buf, buf, 8, None, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "null" in msg
+
+
 STRUCTS = {"Constants": "dak_constants", "LinearArgs": "dak_linear_args", "AllReduceArgs": "dak_allreduce_args",
            "AttnDecodeArgs": "dak_attn_decode_args", "AttnPagedArgs": "dak_attn_paged_args",
            "KvAppendArgs": "dak_kv_append_args"}

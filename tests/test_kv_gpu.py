@@ -188,3 +188,48 @@ def test_paged_attention_bounds_table_entries(host_pool):
             V[b, :, j * P:(j + 1) * P] = vdn[e] if e >= 0 else vhn[-1 - e]
     ref = oracle.decode_attention(q.numpy()[:, :, None, :], K, V, None, 1 / math.sqrt(D))[:, 0]
     assert rel_err(out.float().cpu().numpy(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_fused_rope_append_matches_rope_then_append(dtype):
+    """dak_rope_kv_append writes q_out and every pool byte exactly as dak_rope_qk
+    followed by dak_kv_append_paged do, with pages in both tiers; a bad table
+    entry is recorded in the error word and nothing is written for it."""
+    from directaccesskernel_b200 import _lib, runtime
+    from directaccesskernel_b200.attention import kv_append_paged, rope_kv_append
+    from directaccesskernel_b200.decode_ops import rope_qk
+
+    B, Hq, Hkv, P, D = 5, 8, 2, 16, 128
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, generator=g, device="cuda").to(dtype)
+    inv_freq = 1.0 / (500000.0 ** (torch.arange(0, D, 2, dtype=torch.int64).float().cuda() / D))
+    table = torch.tensor([[0, -1, 3], [-2, 1, -5], [4, -3, 2], [-4, -5, 0], [1, 2, -1]], dtype=torch.int32,
+                         device="cuda")
+    pos = torch.tensor([20, 2, 40, 10, 33], dtype=torch.int32, device="cuda")
+    ref = _pools(5, 5, Hkv, P, D, dtype, seed=3)
+    got = [t.clone() if t.is_cuda else t.clone().pin_memory() for t in ref]
+    q_ref = torch.empty(B, Hq, D, dtype=dtype, device="cuda")
+    k_new = torch.empty(B, Hkv, D, dtype=dtype, device="cuda")
+    v_new = torch.empty_like(k_new)
+    rope_qk(qkv, pos, inv_freq, Hq, Hkv, D, q_ref, k_new, v_new)
+    kv_append_paged(k_new, v_new, *ref, table, pos)
+    q_got = torch.empty_like(q_ref)
+    rope_kv_append(qkv, pos, inv_freq, Hq, Hkv, D, q_got, *got, table)
+    torch.cuda.synchronize()
+    assert runtime.device_status() == 0
+    assert torch.equal(q_got, q_ref)
+    for a, b in zip(got, ref):
+        assert torch.equal(a.cpu(), b.cpu())
+    # An entry past its pool is recorded and skipped; both paths leave the
+    # same bytes (sequence 1's token would land on host page 8 of 5).
+    bad = table.clone()
+    bad[1, 0] = -9
+    k_new2, v_new2 = torch.empty_like(k_new), torch.empty_like(v_new)
+    rope_qk(qkv, pos + 1, inv_freq, Hq, Hkv, D, q_ref, k_new2, v_new2)
+    kv_append_paged(k_new2, v_new2, *ref, bad, pos + 1)
+    assert runtime.device_status(clear=True) == _lib.DAK_ERR_INVALID_ARG
+    rope_kv_append(qkv, pos + 1, inv_freq, Hq, Hkv, D, q_got, *got, bad)
+    assert runtime.device_status(clear=True) == _lib.DAK_ERR_INVALID_ARG
+    assert torch.equal(q_got, q_ref)
+    for a, b in zip(got, ref):
+        assert torch.equal(a.cpu(), b.cpu())
