@@ -282,7 +282,6 @@ def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_de
     return out
 
 
-@traced
 def _kv_append_args(B: int, Hkv: int, D: int, dtype: torch.dtype, k_pool_dev, v_pool_dev, k_pool_host, v_pool_host,
                     block_table: torch.Tensor, positions: torch.Tensor):
     """Checked KvAppendArgs for the paged pools (the layout of ``decode_paged``)."""
@@ -317,6 +316,7 @@ def _kv_append_args(B: int, Hkv: int, D: int, dtype: torch.dtype, k_pool_dev, v_
     return a
 
 
+@traced
 def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.Tensor | None,
                     v_pool_dev: torch.Tensor | None, k_pool_host: torch.Tensor | None,
                     v_pool_host: torch.Tensor | None, block_table: torch.Tensor, positions: torch.Tensor) -> None:
@@ -337,6 +337,7 @@ def kv_append_paged(k_new: torch.Tensor, v_new: torch.Tensor, k_pool_dev: torch.
     check(LIB.dak_kv_append_paged(ctypes.byref(a), _stream_ptr()), "kv_append_paged")
 
 
+@traced
 def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, q_heads: int, kv_heads: int,
                    head_dim: int, q_out: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_dev: torch.Tensor | None,
                    k_pool_host: torch.Tensor | None, v_pool_host: torch.Tensor | None,

@@ -92,6 +92,15 @@ def _bench(args, env_extra=None, timeout=300):
     return [json.loads(ln) for ln in lines]
 
 
+def bench_config():
+    import argparse
+
+    import bench
+
+    args = argparse.Namespace(workload="linear", tokens=None, ratios=None)
+    return bench.linear_metric_config(*bench.linear_sweep(args), 1)[1]
+
+
 def test_reference_arm_prints_one_contract_line():
     """`bench.py --impl reference` (the driver's reference arm): one JSON line on
     this arm's metric and unit, with the CPU baseline it timed and an e2e entry
@@ -101,7 +110,11 @@ def test_reference_arm_prints_one_contract_line():
     assert line["metric"].startswith("offloaded GEMV effective weight GB/s")
     assert line["value"] > 0 and line["steps"] == 1
     cpu = line["cpu_baseline"]
-    assert cpu["kind"] == "port" and cpu["cores"] >= 1 and cpu["value"] == line["value"] and cpu["sample"]
+    # The reference's own computation (torch F.linear on FP32 copies), with the
+    # oracle port's figure beside it; the same config as the GPU arm's line.
+    assert cpu["kind"] == "reference" and cpu["cores"] >= 1 and cpu["value"] == line["value"] and cpu["sample"]
+    assert "F.linear" in cpu["sample"] and cpu["port_value"] > 0
+    assert line["config"] == bench_config()
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
