@@ -346,6 +346,7 @@ bool decode_pdl_enabled() {
 // ---------------------------------------------------------- the split linear
 namespace {
 constexpr int kAutoHostCtas = 8;  // two CTAs with 4 x 32 KB in flight already saturate PCIe Gen5
+constexpr int kMinSplitRows = 1536;  // K rows each CTA of a split keeps at least (12 stages)
 constexpr int kCoreMaxKsplit = 8;
 constexpr int kMmaMaxKsplitHost = 4;
 
@@ -593,12 +594,16 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
       ph = auto_plan(hb, tiles_h, nkb, ks_cap);
       cluster = ph.ksplit;
       if (tiles_d > 0) {
-        // Device-tier plan, from measurements of these kernels on B200: give
-        // each group whole tiles (full-width stages stream fastest) and split
-        // K only as far as needed to bring about 1 MB of weight per CTA (at
-        // least 64 CTAs), because every split adds a DSMEM reduction per tile.
-        // With at least 3/4 of a wave of tiles, no split: tiles are spread
-        // evenly over the resident CTAs.
+        // Device-tier plan, from launch-plan sweeps of these kernels on B200
+        // (the Llama-3-8B layers and one TP8 rank's Llama-3-70B layers, chained
+        // in CUDA graphs): give each group whole tiles (full-width stages
+        // stream fastest) and split K only as far as needed to bring about
+        // 1 MB of weight per CTA (at least 96 CTAs), because every split adds
+        // a DSMEM reduction per tile.  A split never leaves a CTA fewer than
+        // kMinSplitRows K rows, and it stops at a balanced plan within 3/4 of
+        // the target rather than take one that gives some groups two tiles
+        // and others one.  With at least 3/4 of a wave of tiles, no split:
+        // tiles are spread evenly over the resident CTAs.
         long best_cost = -1;
         TierPlan best;
         int best_cluster = cluster;
@@ -615,12 +620,14 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
           best_cluster = 1;
           best_cost = 0;
         } else {
-          const int target = std::max(64, (int)(w_bytes / 1.0e6));
-          for (int ks = 1; ks <= ks_cap && ks <= std::max(1, nkb); ks *= 2) {
+          const int target = std::max(96, (int)(w_bytes / 1.0e6));
+          const int ks_rows = std::max(1, (int)(a->K / kMinSplitRows));
+          for (int ks = 1; ks <= ks_cap && ks <= std::max(1, nkb) && (ks == 1 || ks <= ks_rows); ks *= 2) {
             const int cl = std::max(ks, ph.ksplit);
             const int cap = capacity(cl) - (ph.ctas + cl - 1) / cl * cl;
             const int groups = std::min(cap / ks, tiles_full);
             if (groups <= 0) continue;
+            if (best_cost >= 0 && groups < tiles_full && 4 * best.ctas >= 3 * target) break;
             best.ksplit = ks;
             best.ctas = groups * ks;
             best_cluster = cl;
