@@ -126,6 +126,7 @@ SIGNATURES = {
     "dak_flush_l2_cache": (c_int, [c_vp, ctypes.c_size_t, c_vp, c_vp]),
     "dak_attn_decode": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_attn_decode_paged": (c_int, [ctypes.POINTER(AttnPagedArgs), c_vp]),
+    "dak_attn_decode_paged_merged": (c_int, [ctypes.POINTER(AttnPagedArgs), c_vp, c_vp]),
     "dak_kv_append_paged": (c_int, [ctypes.POINTER(KvAppendArgs), c_vp]),
     "dak_rope_kv_append": (c_int, [c_vp, c_i64, c_vp, c_vp, c_int, ctypes.POINTER(KvAppendArgs), c_vp]),
     "dak_linear_split_allreduce": (c_int, [ctypes.POINTER(LinearArgs), ctypes.POINTER(AllReduceArgs), c_vp]),

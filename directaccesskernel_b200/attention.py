@@ -214,13 +214,17 @@ def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_de
                  k_pool_host: torch.Tensor | None, v_pool_host: torch.Tensor | None, block_table: torch.Tensor,
                  seq_lens: torch.Tensor, scaling: float, split_size: int | None = None, *,
                  out: torch.Tensor | None = None, partial_o: torch.Tensor | None = None,
-                 partial_ml: torch.Tensor | None = None, max_seq_len: int | None = None) -> torch.Tensor:
+                 partial_ml: torch.Tensor | None = None, max_seq_len: int | None = None,
+                 merge_counters: torch.Tensor | None = None) -> torch.Tensor:
     """Decode attention over paged KV; returns [B, Hq, D].
 
     Pools are [pages, Hkv, page_size, D] (one in HBM, one in pinned host
     memory); ``block_table`` [B, max_pages] int32 on the GPU names page j of
     sequence b as v >= 0 (device page v) or v < 0 (host page -1 - v);
-    ``seq_lens`` [B] int32 on the GPU."""
+    ``seq_lens`` [B] int32 on the GPU.  With ``merge_counters`` (int32 CUDA,
+    B * Hkv entries, zero before the first call and left zero by every call)
+    the last split of each (sequence, KV head) merges the splits inside the
+    attention kernel instead of a second launch; the result is the same."""
     if query.dim() != 3 or query.size(2) != HEAD_DIM or query.stride(2) != 1:
         raise RuntimeError("query must be [B, Hq, 128] with a contiguous last dimension")
     if query.dtype not in (torch.float16, torch.bfloat16):
@@ -278,7 +282,14 @@ def decode_paged(query: torch.Tensor, k_pool_dev: torch.Tensor | None, v_pool_de
     # Page counts let the kernel bound every table entry (out of range: zeros + error word).
     a.dev_pages = k_pool_dev.size(0) if k_pool_dev is not None else 0
     a.host_pages = k_pool_host.size(0) if k_pool_host is not None else 0
-    check(LIB.dak_attn_decode_paged(ctypes.byref(a), _stream_ptr()), "decode_paged")
+    if merge_counters is not None:
+        if merge_counters.dtype != torch.int32 or not merge_counters.is_cuda or merge_counters.numel() < B * Hkv \
+                or not merge_counters.is_contiguous():
+            raise RuntimeError("merge_counters must be a contiguous int32 CUDA tensor of batch * Hkv entries")
+        check(LIB.dak_attn_decode_paged_merged(ctypes.byref(a), merge_counters.data_ptr(), _stream_ptr()),
+              "decode_paged")
+    else:
+        check(LIB.dak_attn_decode_paged(ctypes.byref(a), _stream_ptr()), "decode_paged")
     return out
 
 

@@ -58,6 +58,7 @@ struct alignas(64) AttnParams {
   float scaling;
   int *status;
   int pdl;                 // launched with programmatic stream serialization
+  int *merge_counters;     // [batch * num_kv_heads]: the last split merges (nullptr: merge kernel)
   int check_pages;         // paged mode: bound table entries by pages[]
   long long pages[2];      // paged mode: pages in the [0] host, [1] device pool (0: no pool)
 };
@@ -141,6 +142,86 @@ __device__ __forceinline__ PageLoc locate(const AttnParams &p, int b, int tok0) 
     l.row = tok0;
   }
   return l;
+}
+
+// Log-sum-exp merge of the split partials (opt_attention_kernel.cuh:362-386).
+// Both merge paths below compute, for each head, in split order and with the
+// same fused multiply-adds:
+//   gm = max_s m_s,  c_s = exp(m_s - gm) (0 for an empty split),
+//   den = sum_s l_s c_s,  out_d = (sum_s o_{s,d} c_s) / den (0 when den == 0),
+// so the separate merge kernel and the in-kernel merge give the same bits.
+// The partials are read through L2: other CTAs wrote them.
+__device__ __forceinline__ float merge_scale(float m, float gm) {
+  return (m == -FLT_MAX || gm == -FLT_MAX) ? 0.f : expf(m - gm);
+}
+
+// One query head per CTA, dim d per thread (the merge kernel).
+template <typename T>
+__device__ __forceinline__ void merge_one_head(const AttnParams &p, int b, int hq, int d) {
+  const long long base = ((long long)b * p.num_q_heads + hq) * p.num_splits;
+  float gm = -FLT_MAX;
+  for (int s = 0; s < p.num_splits; ++s) gm = fmaxf(gm, __ldcg(p.partial_ml + (base + s) * 2));
+  float den = 0.f, acc = 0.f;
+  for (int s = 0; s < p.num_splits; ++s) {
+    const float c = merge_scale(__ldcg(p.partial_ml + (base + s) * 2), gm);
+    den = __fmaf_rn(__ldcg(p.partial_ml + (base + s) * 2 + 1), c, den);
+    acc = __fmaf_rn(__ldcg(p.partial_o + (base + s) * kHeadDim + d), c, acc);
+  }
+  uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + (long long)b * p.o_stride_b + (long long)hq * p.o_stride_h;
+  out[d] = Elem<T>::from_float(den == 0.f ? 0.f : acc / den);
+}
+
+// Shared-memory floats the in-kernel merge of G heads over `splits` needs:
+// (m, l) pairs, scales and one denominator per head.
+__host__ __device__ constexpr long long merge_stage_floats(int G, long long splits) {
+  return 3 * G * splits + G;
+}
+
+// The G query heads of KV head kvh of sequence b, by the 128 compute threads
+// of the CTA that finished last, with `stage` (shared memory) for the (m, l)
+// pairs and scales.  The pairs arrive in one parallel load, one thread per
+// head turns them into scales, and each thread then sums its dim of all G
+// heads with G independent loads per split, so the merge costs a few L2 round
+// trips rather than one per split and head.
+template <typename T, int G>
+__device__ __forceinline__ void merge_group(const AttnParams &p, int b, int kvh, float *stage) {
+  const int S = p.num_splits;
+  const int tid = threadIdx.x;
+  float *ml = stage;             // [G][S][2]
+  float *sc = stage + 2 * G * S; // [G][S]
+  float *den = sc + G * S;       // [G]
+  // Heads kvh*G .. kvh*G+G-1 of sequence b are contiguous in the partials.
+  const long long base = ((long long)b * p.num_q_heads + (long long)kvh * G) * S;
+  for (int i = tid; i < 2 * G * S; i += kAttnComputeWarps * 32) ml[i] = __ldcg(p.partial_ml + base * 2 + i);
+  named_sync(1, kAttnComputeWarps * 32);
+  if (tid < G) {
+    const float *mg = ml + (long long)tid * S * 2;
+    float gm = -FLT_MAX;
+    for (int s = 0; s < S; ++s) gm = fmaxf(gm, mg[2 * s]);
+    float dn = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float c = merge_scale(mg[2 * s], gm);
+      sc[tid * S + s] = c;
+      dn = __fmaf_rn(mg[2 * s + 1], c, dn);
+    }
+    den[tid] = dn;
+  }
+  named_sync(1, kAttnComputeWarps * 32);
+  const int d = tid;
+  const float *po = p.partial_o + base * kHeadDim + d;
+  float acc[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) acc[g] = 0.f;
+#pragma unroll 2
+  for (int s = 0; s < S; ++s) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      acc[g] = __fmaf_rn(__ldcg(po + ((long long)g * S + s) * kHeadDim), sc[g * S + s], acc[g]);
+  }
+  uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + (long long)b * p.o_stride_b;
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    out[(long long)(kvh * G + g) * p.o_stride_h + d] = Elem<T>::from_float(den[g] == 0.f ? 0.f : acc[g] / den[g]);
 }
 
 template <typename T, int G, int ST>
@@ -431,28 +512,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const __gr
       }
     }
   }
+  if (p.num_splits > 1 && p.merge_counters) {
+    // The last split of this (sequence, KV head) to finish merges all of them:
+    // every CTA publishes its partials, then counts itself; the CTA that
+    // counts last sees every partial and resets the counter for the next call.
+    int *last = reinterpret_cast<int *>(smem + S::flag_off + 8);
+    __threadfence();
+    named_sync(1, kAttnComputeWarps * 32);
+    if (threadIdx.x == 0) {
+      int *counter = p.merge_counters + (long long)b * p.num_kv_heads + kvh;
+      *last = atomicAdd(counter, 1) == p.num_splits - 1 ? 1 : 0;
+      if (*last) *counter = 0;
+    }
+    named_sync(1, kAttnComputeWarps * 32);
+    if (*last) {
+      __threadfence();
+      // The ring is free: every thread is past its last read of ored.
+      merge_group<T, G>(p, b, kvh, reinterpret_cast<float *>(smem + S::kv_off));
+    }
+  }
 }
 
 // Log-sum-exp merge of the splits (opt_attention_kernel.cuh:362-386).
 template <typename T>
 __global__ void __launch_bounds__(kHeadDim) attn_merge_kernel(const __grid_constant__ AttnParams p) {
   pdl_enter(p.pdl);
-  const int hq = blockIdx.x % p.num_q_heads;
-  const int b = blockIdx.x / p.num_q_heads;
-  const int d = threadIdx.x;
-  const long long base = ((long long)b * p.num_q_heads + hq) * p.num_splits;
-  float gm = -FLT_MAX;
-  for (int s = 0; s < p.num_splits; ++s) gm = fmaxf(gm, p.partial_ml[(base + s) * 2]);
-  float den = 0.f, acc = 0.f;
-  for (int s = 0; s < p.num_splits; ++s) {
-    const float m = p.partial_ml[(base + s) * 2];
-    const float l = p.partial_ml[(base + s) * 2 + 1];
-    const float sc = (m == -FLT_MAX || gm == -FLT_MAX) ? 0.f : expf(m - gm);
-    den += l * sc;
-    acc += p.partial_o[(base + s) * kHeadDim + d] * sc;
-  }
-  uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + (long long)b * p.o_stride_b + (long long)hq * p.o_stride_h;
-  out[d] = Elem<T>::from_float(den == 0.f ? 0.f : acc / den);
+  merge_one_head<T>(p, blockIdx.x / p.num_q_heads, blockIdx.x % p.num_q_heads, threadIdx.x);
 }
 
 template <typename T, int G, int ST>
@@ -463,7 +548,7 @@ cudaError_t launch_g(const AttnParams &p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   const int grid = p.batch * p.num_kv_heads * p.num_splits;
   e = launch_ex(kern, dim3(grid), dim3(kAttnThreads), smem, stream, 1, p.pdl != 0, p);
-  if (e != cudaSuccess || p.num_splits == 1) return e;
+  if (e != cudaSuccess || p.num_splits == 1 || p.merge_counters) return e;
   return launch_ex(attn_merge_kernel<T>, dim3(p.batch * p.num_q_heads), dim3(kHeadDim), 0, stream, 1, p.pdl != 0, p);
 }
 
@@ -620,7 +705,13 @@ int dak_attn_decode(const dak_attn_decode_args *a, void *stream) {
   return cuda_status(e, "attention launch");
 }
 
-int dak_attn_decode_paged(const dak_attn_paged_args *a, void *stream) {
+}  // extern "C"
+
+namespace dak {
+namespace {
+// Both paged entry points: with merge_counters the last split of each
+// (sequence, KV head) merges the partials inside the attention kernel.
+int attn_paged(const dak_attn_paged_args *a, int32_t *merge_counters, void *stream) {
   if (!a) return fail(DAK_ERR_INVALID_ARG, "args is null");
   int group, st;
   if ((st = common_checks(a->batch, a->num_q_heads, a->num_kv_heads, a->head_dim, a->split_size, a->dtype, &group)))
@@ -683,9 +774,35 @@ int dak_attn_decode_paged(const dak_attn_paged_args *a, void *stream) {
   p.scaling = a->scaling;
   p.status = device_status_word();
   if (!p.status) return fail(DAK_ERR_CUDA, "no device status word");
+  if (merge_counters && splits > 1) {
+    if ((reinterpret_cast<uintptr_t>(merge_counters) & 3u) != 0)
+      return fail(DAK_ERR_ALIGNMENT, "merge_counters must be 4-byte aligned");
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, merge_counters) != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return fail(DAK_ERR_INVALID_ARG, "merge_counters must be device memory of the current device");
+    }
+    // A merge whose (m, l) pairs and scales do not fit the ring (more than
+    // about 8K splits x heads per KV head) takes the separate merge kernel
+    // and leaves the counters untouched.
+    if (merge_stage_floats(group, splits) * 4 <= (long long)kAttnStages * kStageBytes) p.merge_counters = merge_counters;
+  }
   cudaError_t e = a->dtype == DAK_DTYPE_F16 ? launch_t<__half>(p, group, static_cast<cudaStream_t>(stream))
                                             : launch_t<__nv_bfloat16>(p, group, static_cast<cudaStream_t>(stream));
   return cuda_status(e, "paged attention launch");
+}
+}  // namespace
+}  // namespace dak
+
+extern "C" {
+
+int dak_attn_decode_paged(const dak_attn_paged_args *a, void *stream) {
+  return dak::attn_paged(a, nullptr, stream);
+}
+
+int dak_attn_decode_paged_merged(const dak_attn_paged_args *a, int32_t *merge_counters, void *stream) {
+  if (!merge_counters) return dak::fail(DAK_ERR_INVALID_ARG, "merge_counters is null");
+  return dak::attn_paged(a, merge_counters, stream);
 }
 
 }  // extern "C"

@@ -270,6 +270,9 @@ class TPLlamaDecoder(nn.Module):
         ns = -(-self.max_ctx // auto_split_size(B, self.hkv, self.max_ctx))
         self.partial_o = torch.empty(B, self.hq, ns, d, dtype=torch.float32, device=self.device)
         self.partial_ml = torch.empty(B, self.hq, ns, 2, dtype=torch.float32, device=self.device)
+        # The last split of each (sequence, KV head) merges in the attention
+        # kernel; every call leaves these counters at zero.
+        self.merge_counters = torch.zeros(B * self.hkv, dtype=torch.int32, device=self.device)
         self.inv_freq = 1.0 / (self.s.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float32, device=self.device) / d))
         self.next_ids = torch.zeros(B, dtype=torch.long, device=self.device)
         self.logits_full = None
@@ -340,7 +343,7 @@ class TPLlamaDecoder(nn.Module):
             with t("attention"):
                 decode_paged(self.q_buf, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale,
                              self.split, out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
-                             max_seq_len=self.max_ctx)
+                             max_seq_len=self.max_ctx, merge_counters=self.merge_counters)
             with t("o" if self.ar is not None else "o+allreduce"):
                 o = self._row_parallel(layer.o, self.attn_out.view(B, qd), self.o_buf)
             with t("allreduce+norm" if self.ar is not None else "norm"):
@@ -415,11 +418,10 @@ class TPLlamaDecoder(nn.Module):
     def kernel_launches_per_step(self) -> int:
         """Launches of this library's kernels in one ``forward_step``: the first
         RMSNorm; per layer the four linears, rotary with the KV append, attention
-        (plus the split merge when a sequence spans several splits), SiLU-gate and
+        (which also merges its splits), SiLU-gate and
         two RMSNorms; then lm_head.  The torch ops around them (embedding gather,
         greedy pick) and NCCL's kernels are not counted."""
-        merge = 1 if -(-self.max_ctx // self.split) > 1 else 0
-        return 1 + len(self.layers) * (9 + merge) + 1
+        return 1 + len(self.layers) * 9 + 1
 
     def advance(self) -> None:
         """Feeds the greedy tokens back and moves every sequence one position on."""

@@ -228,10 +228,14 @@ def linear_split(x: torch.Tensor, y: torch.Tensor, w_host: torch.Tensor | None, 
 
 
 def probe_stream_read(src: torch.Tensor, ctas: int, stages: int = 4, chunk_bytes: int = 32768,
-                      nbytes: int | None = None) -> torch.Tensor:
+                      nbytes: int | None = None, sink: torch.Tensor | None = None) -> torch.Tensor:
     """Streams ``src`` (HBM or pinned host memory) through shared memory with
-    TMA bulk copies; returns the 1-element checksum tensor it writes."""
-    sink = torch.zeros(1, dtype=torch.int32, device="cuda")
+    TMA bulk copies; returns the 1-element int32 checksum tensor it writes
+    (``sink`` when given, so a CUDA graph of probes holds only probe launches)."""
+    if sink is None:
+        sink = torch.zeros(1, dtype=torch.int32, device="cuda")
+    elif sink.dtype != torch.int32 or not sink.is_cuda or sink.numel() < 1:
+        raise RuntimeError("sink must be an int32 CUDA tensor")
     n = src.numel() * src.element_size() if nbytes is None else int(nbytes)
     check(LIB.dak_probe_stream_read(src.data_ptr(), n, ctas, stages, chunk_bytes, sink.data_ptr(), _stream_ptr()),
           "probe_stream_read")

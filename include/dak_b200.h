@@ -311,6 +311,20 @@ typedef struct dak_attn_paged_args {
 } dak_attn_paged_args;
 DAK_API int dak_attn_decode_paged(const dak_attn_paged_args *args, void *stream);
 
+/* dak_attn_decode_paged with the split merge inside the attention kernel: the
+ * last split of each (sequence, KV head) to finish merges every split's
+ * partials, so no second kernel is launched.  merge_counters is caller-owned
+ * device memory of batch * num_kv_heads int32, zero before the first call;
+ * every completed call leaves it zero again.  Calls that share one counter
+ * array must not overlap on the GPU.  Results are the same bits as
+ * dak_attn_decode_paged's (the merge arithmetic is shared).  When
+ * (num_q_heads / num_kv_heads) x splits exceeds about 8,000, the (m, l) pairs
+ * do not fit the kernel's shared memory: the separate merge kernel runs and
+ * the counters are not touched.  No reference
+ * counterpart: the reference always launches a separate merge kernel
+ * (opt_attention_kernel.cu:9-35). */
+DAK_API int dak_attn_decode_paged_merged(const dak_attn_paged_args *args, int32_t *merge_counters, void *stream);
+
 /* Appends one token per sequence to a tiered, paged KV cache: for sequence b
  * and KV head h, k_new[b, h, :] and v_new[b, h, :] go to slot
  * positions[b] % page_size of page block_table[b, positions[b] / page_size],

@@ -209,6 +209,23 @@ def test_rope_kv_append_argument_checks():
     assert st == _lib.DAK_ERR_INVALID_ARG and "null" in msg
 
 
+def test_paged_merged_argument_checks():
+    """The in-kernel-merge entry point needs its counter array, and then checks
+    its arguments as dak_attn_decode_paged does, before any launch."""
+    from directaccesskernel_b200 import _lib
+
+    L = _lib.LIB
+    a = _lib.AttnPagedArgs()
+    st, msg = _status(L.dak_attn_decode_paged_merged, ctypes.byref(a), None, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "merge_counters is null" in msg
+    st, msg = _status(L.dak_attn_decode_paged_merged, None, 0x10000, None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "args is null" in msg
+    a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim, a.split_size, a.dtype = 2, 8, 2, 128, 64, _lib.DTYPE_F16
+    a.page_size, a.max_seq_len = 48, 256
+    st, msg = _status(L.dak_attn_decode_paged_merged, ctypes.byref(a), 0x10000, None)
+    assert st == _lib.DAK_ERR_UNSUPPORTED and "page_size" in msg
+
+
 STRUCTS = {"Constants": "dak_constants", "LinearArgs": "dak_linear_args", "AllReduceArgs": "dak_allreduce_args",
            "AttnDecodeArgs": "dak_attn_decode_args", "AttnPagedArgs": "dak_attn_paged_args",
            "KvAppendArgs": "dak_kv_append_args"}

@@ -155,6 +155,63 @@ def test_paged_decode_mixed_tiers(B, Hq, Hkv, seq_lens, P, host_frac, split):
     assert rel_err(out.float().cpu().numpy(), ref) < TOL
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("B,Hq,Hkv,seq_lens,P,host_frac,split", [
+    (2, 8, 2, [1, 333], 16, 0.5, 64),
+    (3, 32, 8, [700, 64, 1025], 16, 0.5, 256),
+    (4, 16, 2, [2048, 1, 999, 1500], 64, 0.3, 192),
+])
+def test_paged_decode_with_in_kernel_merge(B, Hq, Hkv, seq_lens, P, host_frac, split, dtype):
+    """With merge counters the last split of each (sequence, KV head) merges in
+    the attention kernel: the output is bitwise the separate merge kernel's,
+    over several calls in a row and CUDA-graph replays, and the counters are
+    left at zero."""
+    from directaccesskernel_b200 import runtime
+    from directaccesskernel_b200.attention import decode_paged
+
+    s = _paged_setup(B, Hq, Hkv, seq_lens, P, host_frac, seed=B * 11 + P, dtype=dtype)
+    has_dev = (s["table"][s["table"] != 0x7FFFFFFF] >= 0).any()
+    has_host = (s["table"] < 0).any()
+    args = (s["q"].cuda(), s["kd"].cuda() if has_dev else None, s["vd"].cuda() if has_dev else None,
+            s["kh"].pin_memory() if has_host else None, s["vh"].pin_memory() if has_host else None,
+            torch.from_numpy(s["table"]).cuda(), torch.from_numpy(s["seq"]).cuda(), 1.0 / math.sqrt(128), split)
+    ref = decode_paged(*args)
+    counters = torch.zeros(B * Hkv, dtype=torch.int32, device="cuda")
+    out = torch.full_like(ref, float("nan"))
+    for _ in range(3):
+        decode_paged(*args, out=out, merge_counters=counters)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        assert int(counters.abs().sum()) == 0
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side), torch.cuda.graph(graph):
+        decode_paged(*args, out=out, merge_counters=counters)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    assert int(counters.abs().sum()) == 0
+    assert runtime.device_status() == 0
+
+
+def test_in_kernel_merge_rejects_bad_counters():
+    from directaccesskernel_b200.attention import decode_paged
+
+    s = _paged_setup(2, 8, 2, [300, 300], 16, 0.0, seed=5)
+    args = (s["q"].cuda(), s["kd"].cuda(), s["vd"].cuda(), None, None, torch.from_numpy(s["table"]).cuda(),
+            torch.from_numpy(s["seq"]).cuda(), 1.0 / math.sqrt(128), 64)
+    with pytest.raises(RuntimeError, match="merge_counters"):
+        decode_paged(*args, merge_counters=torch.zeros(4, dtype=torch.int64, device="cuda"))
+    with pytest.raises(RuntimeError, match="merge_counters"):
+        decode_paged(*args, merge_counters=torch.zeros(3, dtype=torch.int32, device="cuda"))
+    with pytest.raises(RuntimeError, match="merge_counters"):
+        decode_paged(*args, merge_counters=torch.zeros(4, dtype=torch.int32).pin_memory())
+
+
 def test_hf_hook_decode_through_registry():
     import opt_attention
     from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS

@@ -107,8 +107,8 @@ def test_kernel_launch_count_per_step():
     dec = _cpu_rank(s, 0, 8)
     dec.layers = list(range(20))
     dec.max_ctx, dec.split = 16384 + 64, 1024
-    # Per layer: 4 linears, rotary with the KV append, attention, merge,
-    # SiLU-gate and 2 RMSNorms.
-    assert dec.kernel_launches_per_step() == 1 + 20 * 10 + 1
-    dec.split = dec.max_ctx  # one split: no merge kernel
+    # Per layer: 4 linears, rotary with the KV append, attention (which merges
+    # its own splits), SiLU-gate and 2 RMSNorms.
+    assert dec.kernel_launches_per_step() == 1 + 20 * 9 + 1
+    dec.split = dec.max_ctx  # one split: the same launches
     assert dec.kernel_launches_per_step() == 1 + 20 * 9 + 1
