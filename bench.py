@@ -67,7 +67,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["linear", "prefill", "attention", "opt66b", "llama70b", "plan-sweep"],
+    ap.add_argument("--workload", choices=["linear", "prefill", "attention", "opt66b", "llama70b", "plan-sweep",
+                                           "read-ceiling"],
                     default="linear",
                     help="prefill: the Llama-3-8B layers at 512 tokens, r in {0, 0.5, 1} (large-N path)")
     ap.add_argument("--layers", type=int, default=80, help="llama70b: decoder layers")
@@ -711,6 +712,82 @@ def run_plan_sweep(args, torch, rank, world):
                                     f"HBM x M{tokens}; {copies} weight copies per chain (more than L2)")}}
 
 
+def run_read_ceiling(args, torch, rank, world):
+    """What a launch-separated HBM stream reaches on the four Llama-3-8B weight
+    sizes, one GPU: the library's bandwidth probe (TMA bulk reads into a
+    shared-memory ring, a checksum as the only output) at several launch
+    shapes, against the HBM-only (r = 0) linear kernels at M = 1 on the same
+    bytes, timed the same two ways.  Isolated: one launch at a time, L2 flushed
+    before each.  Chained: the four layers as one CUDA graph of four launches,
+    L2 flushed before the graph; each line of the graph reads its own bytes."""
+    from directaccesskernel_b200 import runtime
+
+    hbm_gbs, peak_kind = measured_peaks()
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    # The linear entry point takes the transposed weight, [K, N] (the layout the modules keep).
+    weights = {name: (torch.randn(k, n, device="cuda") * 0.02).half() for name, (n, k) in LLAMA8B.items()}
+    xs = {name: torch.randn(1, k, device="cuda").half() for name, (n, k) in LLAMA8B.items()}
+    ys = {name: torch.empty(1, n, device="cuda", dtype=torch.float16) for name, (n, k) in LLAMA8B.items()}
+    total = sum(w.numel() * 2 for w in weights.values())
+    sink = torch.zeros(1, dtype=torch.int32, device="cuda")
+    reps = max(3, args.steps)
+
+    def graph_of(calls):
+        for c in calls:
+            c()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side), torch.cuda.graph(g):
+            for c in calls:
+                c()
+        stream.wait_stream(side)
+        return g
+
+    def timed(graph):
+        best = float("inf")
+        for _ in range(max(1, args.warmup)):
+            graph.replay()
+        for _ in range(reps):
+            flush.add_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e-3)
+        return best
+
+    def measure(make_call):
+        calls = [make_call(name) for name in LLAMA8B]
+        iso = sum(timed(graph_of([c])) for c in calls)
+        chained = timed(graph_of(calls))
+        return {"isolated_frac": round(total / iso / 1e9 / hbm_gbs, 3),
+                "chained_frac": round(total / chained / 1e9 / hbm_gbs, 3),
+                "chained_us": round(chained * 1e6, 2)}
+
+    results = []
+    for ctas, stages, chunk in ((runtime.NUM_SMS, 6, 32768), (runtime.NUM_SMS, 12, 16384),
+                                (2 * runtime.NUM_SMS, 6, 16384), (runtime.NUM_SMS, 3, 65536)):
+        r = measure(lambda name, c=ctas, s=stages, ch=chunk: (lambda: runtime.probe_stream_read(
+            weights[name].view(torch.uint8).view(-1), c, s, ch, sink=sink)))
+        results.append({"kernel": "probe_read", "ctas": ctas, "stages": stages, "chunk_bytes": chunk, **r})
+    lin = measure(lambda name: (lambda: runtime.linear_split(xs[name], ys[name], None, weights[name])))
+    results.append({"kernel": "linear (automatic plan), M = 1, r = 0", **lin})
+    if runtime.device_status() != 0:
+        raise RuntimeError("device error word set during the read-ceiling run")
+    best_probe = max(r["chained_frac"] for r in results if r["kernel"] == "probe_read")
+    return {"metric": "HBM read ceiling of launch-separated streams: fraction of measured HBM peak, four "
+                      "Llama-3-8B weight sizes as four launches in one CUDA graph",
+            "value": best_probe, "unit": "fraction of hbm_gbs", "n_gpus": 1, "steps": reps, "warmup": args.warmup,
+            "higher_is_better": True, "linear_chained_frac": lin["chained_frac"],
+            "linear_isolated_frac": lin["isolated_frac"], "shapes": results, "hbm_gbs": hbm_gbs,
+            "hbm_peak_kind": peak_kind, "weight_bytes": total,
+            "config": {"workload": "Llama-3-8B qkv/o/gate_up/down weight bytes (436 MB), L2 flushed before each "
+                                   "timed graph; best of the timed replays"}}
+
+
 class CpuLinearSweep:
     """The sweep's layer calls computed on the host cores, for the CPU baseline
     and the reference arm.  ``impl`` "torch" is the reference's own computation
@@ -1344,7 +1421,7 @@ def main():
               file=sys.stderr, flush=True)
     try:
         fn = {"attention": run_attention, "opt66b": run_opt66b, "llama70b": run_llama70b,
-              "plan-sweep": run_plan_sweep}.get(args.workload, run_linear)
+              "plan-sweep": run_plan_sweep, "read-ceiling": run_read_ceiling}.get(args.workload, run_linear)
         line = fn(args, torch, rank, world)
         if rank == 0:
             print(json.dumps(line), flush=True)
