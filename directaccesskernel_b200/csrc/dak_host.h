@@ -6,6 +6,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <utility>
 
 #include "dak_linear.cuh"
@@ -96,15 +97,16 @@ cudaError_t launch_linear_wide(const LinearParams &p, int dtype, int grid, size_
 // when a captured graph node is launched again on its own.
 cudaError_t prepare_kernel_attributes(const void *kern);
 
-// Launch (or, with grid == 0, occupancy query) of a linear kernel: 1-D grid,
-// 1-D clusters, programmatic stream serialization when p.pdl is set.
+// Launch (or, with grid == 0, occupancy query) of a linear kernel: `grid`
+// CTAs along x (times p.tok_slices rows of token slices along y), 1-D
+// clusters along x, programmatic stream serialization when p.pdl is set.
 template <typename Kern>
 cudaError_t launch_linear_kernel(Kern kern, const LinearParams &p, int grid, int threads, int cluster,
                                  size_t smem, cudaStream_t stream, int *max_clusters) {
   cudaError_t e = prepare_kernel_attributes(reinterpret_cast<const void *>(kern));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid > 0 ? grid : cluster);
+  cfg.gridDim = dim3(grid > 0 ? grid : cluster, grid > 0 ? (unsigned)std::max(1, p.tok_slices) : 1u);
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

@@ -108,6 +108,8 @@ struct alignas(64) LinearParams {
   int pdl;             // launched with programmatic stream serialization: weights are
                        // prefetched before griddepcontrol.wait, x and y only after it
   int ar_on;           // 1: y is the all-reduce (sum over ranks) of this kernel's result
+  int tok_slices;      // tcgen05 kernel: grid rows; row j serves tokens [j * NTOKP, (j+1) * NTOKP)
+                       // of every tile (0 or 1: one row, all tokens)
   ArParams ar;
 };
 

@@ -116,6 +116,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int kb0 = (int)((long long)r * nkb / ks);
   const int kb1 = (int)((long long)(r + 1) * nkb / ks);
   const int feat_per_owner = kMmaBM / ks;  // features each CTA of the group writes
+  // Token slice of this grid row: tokens [tok0, tok0 + NTOKP) of every tile
+  // (grid rows > 1 only without the fused all-reduce).
+  const int tok0 = AR ? 0 : (int)blockIdx.y * NTOKP;
 
   const uint32_t full0 = sbase + L.bar_off;
   const uint32_t empty0 = full0 + S * 8;
@@ -182,7 +185,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       auto x_load = [&](int i, uint32_t fb) {
         const uint32_t xdst = sbase + L.x_off + (i % S) * L.x_stage_bytes;
         for (int h = 0; h < 2; ++h)
-          tma_load_2d(xdst + h * L.x_box_bytes, &p.xmap, (kb0 + i % nk) * kMmaBK + h * 64, 0, fb, pol_x);
+          tma_load_2d(xdst + h * L.x_box_bytes, &p.xmap, (kb0 + i % nk) * kMmaBK + h * 64, tok0, fb, pol_x);
       };
       // Weights do not depend on the previous kernel of the stream: fill the
       // ring with them first, then wait for that kernel before touching x.
@@ -280,7 +283,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         const uint32_t acc_addr = tmem_base + lane_addr + (uint32_t)(ab * NTOKP);
         const int col = tile_box0(j) * kBoxCols + f;
         const bool col_ok = f < tile_nbox(j) * kBoxCols && col < tier.cols;
-        T *ycol = reinterpret_cast<T *>(p.y) + tier.col_offset + col;
+        T *ycol = reinterpret_cast<T *>(p.y) + (long long)tok0 * p.ldy + tier.col_offset + col;
 
         if (ks == 1 || owner == r) {
           if (ks > 1) mbar_wait<true>(red_full, (uint32_t)(nred & 1), wc);
@@ -318,7 +321,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               } else {
 #pragma unroll
                 for (int j = 0; j < kChunkCols; ++j)
-                  if (c0 + j < p.ntok)
+                  if (tok0 + c0 + j < p.ntok)
                     reinterpret_cast<uint16_t *>(ycol)[(long long)(c0 + j) * p.ldy] =
                         Elem<T>::from_float(v[j]);
               }

@@ -570,6 +570,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
     };
     TierPlan ph, pd;
     int cluster = 1;
+    int tok_slices = 1;  // grid rows of tmpl tokens each (tcgen05, HBM-only layers)
     // Largest split factor whose split-K receive buffer still fits with at
     // least two pipeline stages.
     int ks_cap = 1;
@@ -642,6 +643,43 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
         pd = best;
         cluster = best_cluster;
       }
+      // Token slices.  Above 64 tokens a tcgen05 stage holds the activation
+      // rows of every token (64 KB of a 96 KB stage at 256 tokens), so only
+      // two stages fit and the tensor pipe waits on TMA; split-K's receive
+      // buffer does not fit beside them either, so a narrow HBM-only layer
+      // leaves most SMs idle (4096 output features: 32 CTAs).  Grid rows of
+      // 64 or 128 tokens give each CTA smaller stages and more of them, and
+      // the layer more CTAs; the rows read the same weight tiles at about the
+      // same time, mostly from L2.  Taken when a CTA's work (tiles x tokens)
+      // drops by at least a quarter.
+      if (mma && !ar && tiles_h == 0 && pd.ctas > 0 && pd.ksplit == 1 && tmpl >= 128) {
+        const int tiles = (int)(((a->dev_cols + kBoxCols - 1) / kBoxCols + bn / kBoxCols - 1) / (bn / kBoxCols));
+        const long cost0 = (long)((tiles + pd.ctas - 1) / pd.ctas) * tmpl;
+        long best_cost = cost0;
+        int best_w = 0, best_groups = 0, best_rows = 1;
+        for (int sl = 2; sl <= 4 && tmpl / sl >= 64; sl *= 2) {
+          const int w = tmpl / sl;
+          const int rows = (int)((nt + w - 1) / w);
+          const size_t sm = linear_mma_smem_bytes(w, 0);
+          if (sm == 0 || (int)sm > dev->max_smem_optin) continue;
+          const int cap = max_resident_ctas(true, w, a->dtype, 1, sm, dev->num_sms);
+          const int groups = std::min(tiles, cap / rows);
+          if (groups <= 0) continue;
+          const int per = (tiles + groups - 1) / groups;
+          const long cost = (long)per * w;
+          if (4 * cost <= 3 * cost0 && cost < best_cost) {
+            best_cost = cost;
+            best_w = w;
+            best_groups = (tiles + per - 1) / per;
+            best_rows = rows;
+          }
+        }
+        if (best_w > 0) {
+          tmpl = best_w;
+          pd.ctas = best_groups;
+          tok_slices = best_rows;
+        }
+      }
     }
     const int span_h = (ph.ctas + cluster - 1) / cluster * cluster;
     const int span_d = (pd.ctas + cluster - 1) / cluster * cluster;
@@ -649,9 +687,10 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
     if (trace_plans())
       fprintf(stderr,
               "[dak plan] %s ntok=%lld K=%lld host_cols=%lld dev_cols=%lld | host ctas=%d ks=%d | dev ctas=%d ks=%d"
-              " | cluster=%d grid=%d cap=%d\n",
+              " | cluster=%d grid=%d x %d rows of %d tokens | cap=%d\n",
               mma ? "tcgen05" : "core", (long long)nt, (long long)a->K, (long long)a->host_cols,
-              (long long)a->dev_cols, ph.ctas, ph.ksplit, pd.ctas, pd.ksplit, cluster, grid, capacity(cluster));
+              (long long)a->dev_cols, ph.ctas, ph.ksplit, pd.ctas, pd.ksplit, cluster, grid, tok_slices, tmpl,
+              capacity(cluster));
 
     LinearParams p;
     std::memset(&p, 0, sizeof(p));
@@ -684,6 +723,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
     p.status = dev->status;
     p.red_slots = cluster - 1;
     p.pdl = pdl_enabled() ? 1 : 0;
+    p.tok_slices = tok_slices;
     if (ar) {
       if (grid > kArMaxCtas) return fail(DAK_ERR_UNSUPPORTED, "fused all-reduce: grid of %d CTAs", grid);
       if (ar->slot_elems < nt * a->ldy)

@@ -308,3 +308,46 @@ def test_config2_llama8b_sweep(name):
             h_m, _ = split_horizontal((n, k), r)
             y = _split_run(w, x, h_m)
             assert rel_err(y, ref) < TOL, (name, m, r, rel_err(y, ref))
+
+
+@pytest.mark.parametrize("ntok", [65, 128, 200, 256, 512])
+@pytest.mark.parametrize("name", list(LLAMA8B))
+def test_token_sliced_hbm_only_prefill(name, ntok):
+    """HBM-only layers above 64 tokens run as grid rows of 64 or 128 tokens
+    (ragged last row included); every row writes only its own tokens."""
+    n, k = LLAMA8B[name]
+    g = torch.Generator().manual_seed(ntok)
+    w = (torch.randn(n, k, generator=g) * 0.02).half()
+    x = torch.randn(ntok, k, generator=g).half()
+    ref = (x.float() @ w.float().t()).numpy()
+    y = _split_run(w, x, 0)
+    assert not np.isnan(y).any()
+    assert rel_err(y, ref) < TOL, (name, ntok, rel_err(y, ref))
+
+
+def test_token_slices_are_planned(tmp_path):
+    """The plan trace shows the narrow HBM-only layer of 4096 features cut into
+    four 64-token rows at 256 tokens, and no rows when it has host rows."""
+    import os
+    import subprocess
+    import sys
+
+    from conftest import REPO
+
+    code = (
+        "import torch\n"
+        "from directaccesskernel_b200 import runtime\n"
+        "x = torch.randn(256, 1024, device='cuda').half()\n"
+        "w = (torch.randn(1024, 4096) * 0.02).half()\n"
+        "y = torch.empty(256, 4096, device='cuda').half()\n"
+        "runtime.linear_split(x, y, None, w.cuda())\n"
+        "runtime.linear_split(x, y, w[:, :512].contiguous().pin_memory(), w[:, 512:].contiguous().cuda(), 0, 512)\n"
+        "torch.cuda.synchronize()\n"
+        "assert runtime.device_status() == 0\n")
+    env = dict(os.environ, DAK_B200_TRACE_PLAN="1", PYTHONPATH=str(REPO))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0, r.stderr
+    plans = [line for line in r.stderr.splitlines() if line.startswith("[dak plan] tcgen05 ntok=256")]
+    assert len(plans) == 2, r.stderr
+    assert "x 4 rows of 64 tokens" in plans[0], plans[0]
+    assert "x 1 rows of 256 tokens" in plans[1], plans[1]
