@@ -643,34 +643,42 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
         pd = best;
         cluster = best_cluster;
       }
-      // Token slices.  Above 64 tokens a tcgen05 stage holds the activation
-      // rows of every token (64 KB of a 96 KB stage at 256 tokens), so only
-      // two stages fit and the tensor pipe waits on TMA; split-K's receive
-      // buffer does not fit beside them either, so a narrow HBM-only layer
-      // leaves most SMs idle (4096 output features: 32 CTAs).  Grid rows of
-      // 64 or 128 tokens give each CTA smaller stages and more of them, and
-      // the layer more CTAs; the rows read the same weight tiles at about the
-      // same time, mostly from L2.  Taken when a CTA's work (tiles x tokens)
-      // drops by at least a quarter.
+      // Token slices.  Above 64 tokens a CTA's time follows the operand
+      // bytes it moves into shared memory: per K row, a tile of 128 features
+      // brings 256 bytes of weights plus 2 bytes per token of activations.
+      // And split-K's receive buffer no longer fits beside the stages, so a
+      // narrow HBM-only layer would leave most SMs idle (4096 output
+      // features: 32 CTAs).  Grid rows of 64 or 128 tokens give a layer more
+      // CTAs with smaller stages; the rows read the same weight tiles at about
+      // the same time, mostly from L2.  The plan with the fewest bytes for its
+      // busiest CTA wins (by at least 5%); on the Llama-3-8B layers at 256
+      // tokens this model orders the 1-, 2- and 4-row plans as their measured
+      // times do.
       if (mma && !ar && tiles_h == 0 && pd.ctas > 0 && pd.ksplit == 1 && tmpl >= 128) {
-        const int tiles = (int)(((a->dev_cols + kBoxCols - 1) / kBoxCols + bn / kBoxCols - 1) / (bn / kBoxCols));
-        const long cost0 = (long)((tiles + pd.ctas - 1) / pd.ctas) * tmpl;
-        long best_cost = cost0;
+        const int boxes = (int)((a->dev_cols + kBoxCols - 1) / kBoxCols);
+        const int bpt = bn / kBoxCols;
+        auto busiest_cost = [&](int groups, int w) -> long {
+          const int tiles = ((boxes + groups - 1) / groups + bpt - 1) / bpt;  // the busiest group's tiles
+          return (long)tiles * (256 + 2 * w);
+        };
+        long best_cost = busiest_cost(pd.ctas, tmpl);
         int best_w = 0, best_groups = 0, best_rows = 1;
+        const int tiles_all = (boxes + bpt - 1) / bpt;
         for (int sl = 2; sl <= 4 && tmpl / sl >= 64; sl *= 2) {
           const int w = tmpl / sl;
           const int rows = (int)((nt + w - 1) / w);
           const size_t sm = linear_mma_smem_bytes(w, 0);
           if (sm == 0 || (int)sm > dev->max_smem_optin) continue;
           const int cap = max_resident_ctas(true, w, a->dtype, 1, sm, dev->num_sms);
-          const int groups = std::min(tiles, cap / rows);
+          int groups = std::min(tiles_all, cap / rows);
           if (groups <= 0) continue;
-          const int per = (tiles + groups - 1) / groups;
-          const long cost = (long)per * w;
-          if (4 * cost <= 3 * cost0 && cost < best_cost) {
+          const int per = (tiles_all + groups - 1) / groups;
+          groups = (tiles_all + per - 1) / per;  // the fewest groups with that many tiles each
+          const long cost = busiest_cost(groups, w);
+          if (20 * cost < 19 * best_cost) {
             best_cost = cost;
             best_w = w;
-            best_groups = (tiles + per - 1) / per;
+            best_groups = groups;
             best_rows = rows;
           }
         }

@@ -325,9 +325,22 @@ def test_token_sliced_hbm_only_prefill(name, ntok):
     assert rel_err(y, ref) < TOL, (name, ntok, rel_err(y, ref))
 
 
+@pytest.mark.parametrize("ntok", [256, 250])
+@pytest.mark.parametrize("n_out,k", [(28864, 1024), (38464, 512), (4096 + 64, 1024)])
+def test_hbm_only_multi_tile_ctas(n_out, k, ntok):
+    """256-token HBM-only launches whose CTAs hold two or three tiles, the last
+    of one 64-feature box, and a narrow layer that gets token rows."""
+    w, x = _inputs(n_out, k, ntok, seed=n_out + ntok)
+    ref = _oracle(w, x)
+    y = _split_run(w, x, 0)
+    assert not np.isnan(y).any()
+    assert rel_err(y, ref) < TOL, rel_err(y, ref)
+
+
 def test_token_slices_are_planned(tmp_path):
     """The plan trace shows the narrow HBM-only layer of 4096 features cut into
-    four 64-token rows at 256 tokens, and no rows when it has host rows."""
+    four 64-token rows at 256 tokens, no rows when it has host rows, and a wide
+    HBM-only layer (224 tiles) left whole."""
     import os
     import subprocess
     import sys
@@ -342,12 +355,15 @@ def test_token_slices_are_planned(tmp_path):
         "y = torch.empty(256, 4096, device='cuda').half()\n"
         "runtime.linear_split(x, y, None, w.cuda())\n"
         "runtime.linear_split(x, y, w[:, :512].contiguous().pin_memory(), w[:, 512:].contiguous().cuda(), 0, 512)\n"
+        "wide = (torch.randn(1024, 28672, device='cuda') * 0.02).half()\n"
+        "runtime.linear_split(x, torch.empty(256, 28672, device='cuda').half(), None, wide)\n"
         "torch.cuda.synchronize()\n"
         "assert runtime.device_status() == 0\n")
     env = dict(os.environ, DAK_B200_TRACE_PLAN="1", PYTHONPATH=str(REPO))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
     assert r.returncode == 0, r.stderr
     plans = [line for line in r.stderr.splitlines() if line.startswith("[dak plan] tcgen05 ntok=256")]
-    assert len(plans) == 2, r.stderr
-    assert "x 4 rows of 64 tokens" in plans[0], plans[0]
-    assert "x 1 rows of 256 tokens" in plans[1], plans[1]
+    assert len(plans) == 3, r.stderr
+    assert "x 4 rows of 64 tokens |" in plans[0], plans[0]
+    assert "x 1 rows of 256 tokens |" in plans[1], plans[1]
+    assert "x 1 rows of 256 tokens |" in plans[2], plans[2]
