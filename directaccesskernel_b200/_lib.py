@@ -123,6 +123,7 @@ SIGNATURES = {
     "dak_gemv_horizontal_multicast": (c_int, [c_vp, c_vp, c_vp, c_vp] + [c_int] * 9 + [c_vp]),
     "dak_gemv_horizontal_multicast_prefill": (c_int, [c_vp, c_vp, c_vp, c_vp] + [c_int] * 9 + [c_vp]),
     "dak_linear_split": (c_int, [ctypes.POINTER(LinearArgs), c_vp]),
+    "dak_linear_split_glu": (c_int, [ctypes.POINTER(LinearArgs), c_vp]),
     "dak_flush_l2_cache": (c_int, [c_vp, ctypes.c_size_t, c_vp, c_vp]),
     "dak_attn_decode": (c_int, [ctypes.POINTER(AttnDecodeArgs), c_vp]),
     "dak_attn_decode_paged": (c_int, [ctypes.POINTER(AttnPagedArgs), c_vp]),

@@ -110,6 +110,8 @@ struct alignas(64) LinearParams {
   int ar_on;           // 1: y is the all-reduce (sum over ranks) of this kernel's result
   int tok_slices;      // tcgen05 kernel: grid rows; row j serves tokens [j * NTOKP, (j+1) * NTOKP)
                        // of every tile (0 or 1: one row, all tokens)
+  int glu;             // tcgen05 kernel: y = silu(gate) * up of gate/up rows interleaved in
+                       // 16-feature blocks (y has half the weight's output features)
   ArParams ar;
 };
 

@@ -302,7 +302,20 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                 }
               }
             }
-            if (col_ok) {
+            if (!AR && p.glu) {
+              // Gated output: gate and up rows alternate in blocks of 16
+              // features, so lane l < 16 holds gate feature g of this block
+              // and lane l + 16 the matching up feature; y column
+              // (c / 32) * 16 + c % 16 gets silu(gate) * up, rounded once.
+              const int c = tier.col_offset + col;
+              uint16_t *yg = reinterpret_cast<uint16_t *>(p.y) + (long long)tok0 * p.ldy + (c >> 5) * 16 + (c & 15);
+#pragma unroll
+              for (int j = 0; j < kChunkCols; ++j) {
+                const float up = __shfl_xor_sync(0xffffffffu, v[j], 16);
+                if (col_ok && lane < 16 && tok0 + c0 + j < p.ntok)
+                  yg[(long long)(c0 + j) * p.ldy] = Elem<T>::from_float(v[j] / (1.f + expf(-v[j])) * up);
+              }
+            } else if (col_ok) {
               if (AR) {
                 const long long base = ar_slot + tier.col_offset + col;
                 if (p.ar.mc) {

@@ -491,7 +491,7 @@ int run_linear_wide_chunk(const dak_linear_args *a, const DeviceInfo *dev, int64
   return e == cudaSuccess ? DAK_OK : cuda_status(e, "wide linear kernel launch");
 }
 
-int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar = nullptr) {
+int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar = nullptr, bool glu = false) {
   if (!a) return fail(DAK_ERR_INVALID_ARG, "args is null");
   if (a->dtype != DAK_DTYPE_F16 && a->dtype != DAK_DTYPE_BF16)
     return fail(DAK_ERR_UNSUPPORTED, "linear supports float16 and bfloat16 only");
@@ -517,7 +517,10 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
     if ((st = check_ptr16(tiers_w[t], nm))) return st;
     if (tiers_ld[t] < tiers_cols[t] || (tiers_ld[t] % 8) != 0)
       return fail(DAK_ERR_ALIGNMENT, "%s row stride must be >= its columns and a multiple of 8", nm);
-    if (tiers_off[t] < 0 || tiers_off[t] + tiers_cols[t] > a->ldy)
+    if (glu && (tiers_cols[t] % 32 != 0 || tiers_off[t] % 32 != 0))
+      return fail(DAK_ERR_INVALID_ARG, "gated linear: %s columns and offset must be multiples of 32", nm);
+    // A gated linear writes half as many y columns as the weight has features.
+    if (tiers_off[t] < 0 || (tiers_off[t] + tiers_cols[t]) / (glu ? 2 : 1) > a->ldy)
       return fail(DAK_ERR_INVALID_ARG, "%s columns fall outside y", nm);
   }
 
@@ -526,10 +529,11 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
 
   int path = a->path;
   if (path == DAK_PATH_AUTO) path = a->ntok <= kCoreAutoMaxTok ? DAK_PATH_CUDA_CORE : DAK_PATH_TCGEN05;
-  if (ar) {
-    // The fused all-reduce lives in the tcgen05 kernel, which serves any token count.
+  if (ar || glu) {
+    // The fused all-reduce and the gated epilogue live in the tcgen05 kernel,
+    // which serves any token count.
     if (a->path == DAK_PATH_CUDA_CORE)
-      return fail(DAK_ERR_UNSUPPORTED, "the fused all-reduce runs on the tcgen05 path");
+      return fail(DAK_ERR_UNSUPPORTED, "the %s runs on the tcgen05 path", ar ? "fused all-reduce" : "gated linear");
     path = DAK_PATH_TCGEN05;
   }
   if (path == DAK_PATH_CUDA_CORE && a->ntok > kCoreMaxTok)
@@ -543,7 +547,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
   // Token chunks: the tcgen05 kernel serves up to 256 tokens per launch; the
   // wide kernel up to 512 for a layer with host-resident rows, so that those
   // rows cross the host link once per 512 tokens instead of once per 256.
-  const bool wide = mma && !ar && a->host_cols > 0 && a->ntok > kMmaMaxTok;
+  const bool wide = mma && !ar && !glu && a->host_cols > 0 && a->ntok > kMmaMaxTok;
   const int64_t chunk = wide ? 2 * kMmaMaxTok : mma ? kMmaMaxTok : kCoreMaxTok;
   for (int64_t t0 = 0; t0 < a->ntok; t0 += chunk) {
     const int64_t nt = std::min(chunk, a->ntok - t0);
@@ -732,6 +736,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
     p.red_slots = cluster - 1;
     p.pdl = pdl_enabled() ? 1 : 0;
     p.tok_slices = tok_slices;
+    p.glu = glu ? 1 : 0;
     if (ar) {
       if (grid > kArMaxCtas) return fail(DAK_ERR_UNSUPPORTED, "fused all-reduce: grid of %d CTAs", grid);
       if (ar->slot_elems < nt * a->ldy)
@@ -1039,6 +1044,10 @@ int dak_tensormap_replace_address(void *desc, const void *new_base) {
 
 int dak_linear_split(const dak_linear_args *args, void *stream) {
   return run_linear(args, static_cast<cudaStream_t>(stream));
+}
+
+int dak_linear_split_glu(const dak_linear_args *args, void *stream) {
+  return run_linear(args, static_cast<cudaStream_t>(stream), nullptr, true);
 }
 
 int dak_linear_split_allreduce(const dak_linear_args *args, const dak_allreduce_args *ar, void *stream) {

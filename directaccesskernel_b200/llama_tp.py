@@ -157,7 +157,28 @@ class TPLlamaDecoder(nn.Module):
         g = full["gate"][r * self.ffn_r:(r + 1) * self.ffn_r]
         u = full["up"][r * self.ffn_r:(r + 1) * self.ffn_r]
         dn = full["down"][:, r * self.ffn_r:(r + 1) * self.ffn_r]
-        return {"qkv": torch.cat([q, k, v], 0), "o": o, "gate_up": torch.cat([g, u], 0), "down": dn}
+        from .runtime import interleave_gate_up
+
+        gate_up = interleave_gate_up(g, u) if self.fuse_glu else torch.cat([g, u], 0)
+        return {"qkv": torch.cat([q, k, v], 0), "o": o, "gate_up": gate_up, "down": dn}
+
+    @property
+    def fuse_glu(self) -> bool:
+        """gate_up's epilogue applies the SiLU gate when the rank's FFN width is a
+        whole number of 16-feature blocks (gate and up rows interleaved)."""
+        return self.__dict__.get("_fuse_glu", self.ffn_r % 16 == 0)
+
+    @fuse_glu.setter
+    def fuse_glu(self, on: bool) -> None:
+        self.__dict__["_fuse_glu"] = bool(on)
+
+    def split_gate_up(self, gu: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """(gate, up) columns of x @ gate_up^T in this decoder's row order."""
+        f = self.ffn_r
+        if not self.fuse_glu:
+            return gu[..., :f], gu[..., f:]
+        blocks = gu.reshape(*gu.shape[:-1], f // 16, 2, 16)
+        return blocks[..., 0, :].reshape(*gu.shape[:-1], f), blocks[..., 1, :].reshape(*gu.shape[:-1], f)
 
     def _add_layer(self, full: dict) -> None:
         sh = self._shard_layer(full, len(self.layers))
@@ -309,19 +330,30 @@ class TPLlamaDecoder(nn.Module):
             return y
         from .runtime import linear_split
 
-        if hasattr(mod, "weight_h"):
-            wh = mod.weight_h if mod.out_features_h > 0 else None
-            wd = mod.weight_d if mod.out_features_d > 0 else None
-        else:
-            wh, wd = (None, mod.weight) if mod.weight.is_cuda else (mod.weight, None)
+        wh, wd = self._tiers(mod)
         return linear_split(x, out, wh, wd, allreduce=self.ar)
+
+    @staticmethod
+    def _tiers(mod: nn.Module) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+        """(host, device) transposed weights of an offloaded module, host rows first."""
+        if hasattr(mod, "weight_h"):
+            return (mod.weight_h if mod.out_features_h > 0 else None,
+                    mod.weight_d if mod.out_features_d > 0 else None)
+        return (None, mod.weight) if mod.weight.is_cuda else (mod.weight, None)
+
+    def _gated(self, mod: nn.Module, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """silu(gate) * up straight from the gate_up kernel's epilogue."""
+        from .runtime import linear_split
+
+        wh, wd = self._tiers(mod)
+        return linear_split(x, out, wh, wd, glu=True)
 
     def forward_step(self, keep_logits: bool = False) -> torch.Tensor:
         """One decode step on the static buffers: embeds ``ids`` at ``pos``, writes
         their K/V, and leaves the greedy tokens in ``next_ids``; advances nothing.
         Per layer: RMSNorm (residual add fused), qkv, rotary and KV append (one
-        kernel), attention, o + all-reduce, RMSNorm, gate_up, SiLU-gate, down +
-        all-reduce."""
+        kernel), attention, o + all-reduce, RMSNorm, gate_up with the SiLU gate in
+        its epilogue (or gate_up, then SiLU-gate), down + all-reduce."""
         from .decode_ops import rmsnorm, silu_mul
 
         s, B, d = self.s, self.B, self.s.head_dim
@@ -348,10 +380,14 @@ class TPLlamaDecoder(nn.Module):
                 o = self._row_parallel(layer.o, self.attn_out.view(B, qd), self.o_buf)
             with t("allreduce+norm" if self.ar is not None else "norm"):
                 x = self._add_norm(o, layer.post_w)
-            with t("gate_up"):
-                gu = layer.gate_up(x)
-            with t("silu"):
-                act = silu_mul(gu, out=self.act_buf)
+            if self.fuse_glu:
+                with t("gate_up+silu"):
+                    act = self._gated(layer.gate_up, x, self.act_buf)
+            else:
+                with t("gate_up"):
+                    gu = layer.gate_up(x)
+                with t("silu"):
+                    act = silu_mul(gu, out=self.act_buf)
             with t("down" if self.ar is not None else "down+allreduce"):
                 dn = self._row_parallel(layer.down, act, self.dn_buf)
             nxt_w = self.layers[l + 1].in_w if l + 1 < len(self.layers) else self.final_w
@@ -417,11 +453,12 @@ class TPLlamaDecoder(nn.Module):
 
     def kernel_launches_per_step(self) -> int:
         """Launches of this library's kernels in one ``forward_step``: the first
-        RMSNorm; per layer the four linears, rotary with the KV append, attention
-        (which also merges its splits), SiLU-gate and
-        two RMSNorms; then lm_head.  The torch ops around them (embedding gather,
-        greedy pick) and NCCL's kernels are not counted."""
-        return 1 + len(self.layers) * 9 + 1
+        RMSNorm; per layer the four linears (gate_up also applies the SiLU gate
+        when ``fuse_glu``, else a SiLU-gate kernel follows), rotary with the KV
+        append, attention (which also merges its splits) and two RMSNorms; then
+        lm_head.  The torch ops around them (embedding gather, greedy pick) and
+        NCCL's kernels are not counted."""
+        return 1 + len(self.layers) * (8 if self.fuse_glu else 9) + 1
 
     def advance(self) -> None:
         """Feeds the greedy tokens back and moves every sequence one position on."""

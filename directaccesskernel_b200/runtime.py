@@ -187,13 +187,16 @@ def _i64(v) -> int:
 def linear_split(x: torch.Tensor, y: torch.Tensor, w_host: torch.Tensor | None, w_dev: torch.Tensor | None,
                  host_col_offset: int = 0, dev_col_offset: int | None = None, *, host_ctas: int = 0,
                  dev_ctas: int = 0, host_ksplit: int = 0, dev_ksplit: int = 0, path: int = _lib.PATH_AUTO,
-                 allreduce=None) -> torch.Tensor:
+                 allreduce=None, glu: bool = False) -> torch.Tensor:
     """y[:, off:off+cols] = x @ w for each tier, with w the transposed weight [K, cols].
 
     ``x`` is [ntok, K] (row-major, last dim contiguous), ``y`` [ntok, ldy];
     ``w_host`` lives in pinned host memory, ``w_dev`` in HBM; either may be None.
     With ``allreduce`` (a ``tp.SymmetricAllReduce``), y is summed over the ranks
-    of its group inside the same kernel (row-parallel layers).
+    of its group inside the same kernel (row-parallel layers).  With ``glu``
+    the weight's features alternate 16 gate and 16 up rows and
+    y[:, (c // 32) * 16 + c % 16] = silu(gate) * up for the pairs (c, c + 16):
+    y has half as many columns (``interleave_gate_up`` builds the layout).
     """
     if x.dim() != 2 or y.dim() != 2 or x.stride(1) != 1 or y.stride(1) != 1:
         raise RuntimeError("x and y must be 2-D with a contiguous last dimension")
@@ -219,12 +222,30 @@ def linear_split(x: torch.Tensor, y: torch.Tensor, w_host: torch.Tensor | None, 
     a.y, a.ldy = y.data_ptr(), y.stride(0)
     a.ntok, a.K, a.dtype = ntok, K, dak_dtype(x.dtype)
     a.host_ctas, a.dev_ctas, a.host_ksplit, a.dev_ksplit, a.path = host_ctas, dev_ctas, host_ksplit, dev_ksplit, path
-    if allreduce is not None:
+    if glu:
+        if allreduce is not None:
+            raise RuntimeError("a gated linear has no fused all-reduce")
+        check(LIB.dak_linear_split_glu(ctypes.byref(a), _stream_ptr()), "linear_split_glu")
+    elif allreduce is not None:
         check(LIB.dak_linear_split_allreduce(ctypes.byref(a), ctypes.byref(allreduce.args(y)), _stream_ptr()),
               "linear_split_allreduce")
     else:
         check(LIB.dak_linear_split(ctypes.byref(a), _stream_ptr()), "linear_split")
     return y
+
+
+GLU_BLOCK = 16  # gate / up rows alternate in blocks of this many features
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[F, K] gate and up weights -> the [2F, K] row order ``linear_split(glu=True)``
+    reads: 16 gate rows, the 16 matching up rows, the next 16 gate rows, ...
+    F must be a multiple of 16."""
+    if gate.shape != up.shape or gate.dim() != 2 or gate.shape[0] % GLU_BLOCK:
+        raise RuntimeError(f"gate and up must be equal [F, K] with F a multiple of {GLU_BLOCK}")
+    f, k = gate.shape
+    return torch.stack([gate.reshape(f // GLU_BLOCK, GLU_BLOCK, k), up.reshape(f // GLU_BLOCK, GLU_BLOCK, k)],
+                       1).reshape(2 * f, k)
 
 
 def probe_stream_read(src: torch.Tensor, ctas: int, stages: int = 4, chunk_bytes: int = 32768,

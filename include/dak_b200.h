@@ -187,6 +187,19 @@ typedef struct dak_linear_args {
 } dak_linear_args;
 DAK_API int dak_linear_split(const dak_linear_args *args, void *stream);
 
+/* Gated linear (a SwiGLU MLP's gate and up projections with their activation):
+ * the weight's output features alternate 16 gate rows and the 16 matching up
+ * rows, and y[t, j] = silu(g_j) * u_j with g_j, u_j = x . W^T for the pair j
+ * (feature c of the weight, with c % 32 < 16, pairs with c + 16 and writes y
+ * column (c / 32) * 16 + c % 16).  Column offsets and counts of both tiers are
+ * in the weight's feature space and must be multiples of 32; y needs
+ * (offset + cols) / 2 columns.  The product is formed in FP32 from the FP32
+ * accumulators and rounded once.  Runs on the tcgen05 kernel (any ntok) with
+ * the same plans as dak_linear_split.  No kernel counterpart in the
+ * reference: the vendored Llama MLP computes act_fn(gate_proj(x)) * up_proj(x)
+ * in torch (app/python/llama/vanila_llama.py:188-209). */
+DAK_API int dak_linear_split_glu(const dak_linear_args *args, void *stream);
+
 /* Row-parallel linear with its all-reduce fused into the same kernel (no
  * reference counterpart; the reference has no multi-GPU path).  Every rank of a
  * tensor-parallel group calls it with the same shapes; y receives the sum over

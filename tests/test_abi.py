@@ -209,6 +209,23 @@ def test_rope_kv_append_argument_checks():
     assert st == _lib.DAK_ERR_INVALID_ARG and "null" in msg
 
 
+def test_gated_linear_argument_checks():
+    """The gated linear needs 32-feature multiples and room for half the
+    features in y; both are checked before any launch."""
+    from directaccesskernel_b200 import _lib
+
+    L = _lib.LIB
+    a = _lib.LinearArgs()
+    a.x = a.y = a.w_dev = 0x10000
+    a.ldx, a.K, a.ntok, a.dtype = 64, 64, 4, _lib.DTYPE_F16
+    a.dev_cols, a.ld_dev, a.ldy = 48, 48, 24
+    st, msg = _status(L.dak_linear_split_glu, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "multiples of 32" in msg
+    a.dev_cols, a.ld_dev, a.ldy = 64, 64, 24
+    st, msg = _status(L.dak_linear_split_glu, ctypes.byref(a), None)
+    assert st == _lib.DAK_ERR_INVALID_ARG and "outside y" in msg
+
+
 def test_paged_merged_argument_checks():
     """The in-kernel-merge entry point needs its counter array, and then checks
     its arguments as dak_attn_decode_paged does, before any launch."""

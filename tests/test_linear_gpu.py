@@ -367,3 +367,32 @@ def test_token_slices_are_planned(tmp_path):
     assert "x 4 rows of 64 tokens |" in plans[0], plans[0]
     assert "x 1 rows of 256 tokens |" in plans[1], plans[1]
     assert "x 1 rows of 256 tokens |" in plans[2], plans[2]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("ntok", [1, 4, 32, 64, 100, 256])
+@pytest.mark.parametrize("f,k", [(3584, 8192), (512, 1024), (48, 200)])
+def test_gated_linear(f, k, ntok, dtype):
+    """linear_split(glu=True) on interleaved gate/up rows: silu(x g^T) * (x u^T)
+    against the oracle, with every row in HBM, the first rows on the host, and
+    every row on the host."""
+    from directaccesskernel_b200 import runtime
+
+    g = torch.Generator().manual_seed(f + ntok)
+    gate = (torch.randn(f, k, generator=g) * 0.02).to(dtype)
+    up = (torch.randn(f, k, generator=g) * 0.02).to(dtype)
+    x = torch.randn(ntok, k, generator=g).to(dtype)
+    xg = oracle.linear(x.float().numpy(), gate.float().numpy(), acc=np.float64)
+    xu = oracle.linear(x.float().numpy(), up.float().numpy(), acc=np.float64)
+    ref = xg / (1.0 + np.exp(-xg)) * xu
+    wt = runtime.interleave_gate_up(gate, up).t().contiguous()  # [K, 2F]
+    for host_cols in (0, 64 if 2 * f > 64 else 0, 2 * f):
+        wh = wt[:, :host_cols].contiguous().pin_memory() if host_cols else None
+        wd = wt[:, host_cols:].contiguous().cuda() if host_cols < 2 * f else None
+        y = torch.full((ntok, f), float("nan"), dtype=dtype, device="cuda")
+        runtime.linear_split(x.cuda(), y, wh, wd, 0, host_cols, glu=True)
+        torch.cuda.synchronize()
+        assert runtime.device_status() == 0
+        got = y.float().cpu().numpy()
+        assert not np.isnan(got).any()
+        assert rel_err(got, ref) < TOL, (host_cols, rel_err(got, ref))

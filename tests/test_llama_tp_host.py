@@ -71,8 +71,8 @@ def test_layer_shards_compose_to_the_full_layer(world):
         k_parts.append(qkv[:, qd:qd + kd])
         v_parts.append(qkv[:, qd + kd:])
         o_sum = o_sum + attn[:, r * qd:(r + 1) * qd] @ sh["o"].T
-        gu = x @ sh["gate_up"].T
-        mlp_sum = mlp_sum + (silu(gu[:, :dec.ffn_r]) * gu[:, dec.ffn_r:]) @ sh["down"].T
+        g, u = dec.split_gate_up(x @ sh["gate_up"].T)
+        mlp_sum = mlp_sum + (silu(g) * u) @ sh["down"].T
         group = s.heads // s.kv_heads
         for i in range(dec.hq):
             assert (r * dec.hq + i) // group // dec.hkv == r
@@ -107,8 +107,12 @@ def test_kernel_launch_count_per_step():
     dec = _cpu_rank(s, 0, 8)
     dec.layers = list(range(20))
     dec.max_ctx, dec.split = 16384 + 64, 1024
-    # Per layer: 4 linears, rotary with the KV append, attention (which merges
-    # its own splits), SiLU-gate and 2 RMSNorms.
-    assert dec.kernel_launches_per_step() == 1 + 20 * 9 + 1
+    # Per layer: 4 linears (gate_up applies the SiLU gate: 3584 FFN features a
+    # rank), rotary with the KV append, attention (which merges its own
+    # splits) and 2 RMSNorms.
+    assert dec.fuse_glu
+    assert dec.kernel_launches_per_step() == 1 + 20 * 8 + 1
     dec.split = dec.max_ctx  # one split: the same launches
+    assert dec.kernel_launches_per_step() == 1 + 20 * 8 + 1
+    dec.fuse_glu = False  # an FFN width that is not whole 16-feature blocks: a SiLU-gate kernel too
     assert dec.kernel_launches_per_step() == 1 + 20 * 9 + 1
