@@ -396,3 +396,39 @@ def test_gated_linear(f, k, ntok, dtype):
         got = y.float().cpu().numpy()
         assert not np.isnan(got).any()
         assert rel_err(got, ref) < TOL, (host_cols, rel_err(got, ref))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_token_slices_and_gated_linear_in_a_cuda_graph(dtype):
+    """Token-sliced launches (down-like: 4 rows of 64 tokens) and the gated
+    linear, captured once in a CUDA graph and replayed on new activations."""
+    from directaccesskernel_b200 import runtime
+
+    g = torch.Generator().manual_seed(21)
+    w = (torch.randn(4096, 1024, generator=g) * 0.02).to(dtype)
+    gate = (torch.randn(512, 1024, generator=g) * 0.02).to(dtype)
+    up = (torch.randn(512, 1024, generator=g) * 0.02).to(dtype)
+    wt = w.t().contiguous().cuda()
+    gt = runtime.interleave_gate_up(gate, up).t().contiguous().cuda()
+    xin = torch.zeros(256, 1024, dtype=dtype, device="cuda")
+    y = torch.empty(256, 4096, dtype=dtype, device="cuda")
+    act = torch.empty(256, 512, dtype=dtype, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        runtime.linear_split(xin, y, None, wt)
+        runtime.linear_split(xin, act, None, gt, glu=True)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        runtime.linear_split(xin, y, None, wt)
+        runtime.linear_split(xin, act, None, gt, glu=True)
+    for seed in (22, 23):
+        x = torch.randn(256, 1024, generator=torch.Generator().manual_seed(seed)).to(dtype)
+        xin.copy_(x.cuda())
+        graph.replay()
+        torch.cuda.synchronize()
+        assert runtime.device_status() == 0
+        assert rel_err(y.float().cpu().numpy(), _oracle(w, x)) < TOL
+        xg, xu = _oracle(gate, x), _oracle(up, x)
+        assert rel_err(act.float().cpu().numpy(), xg / (1.0 + np.exp(-xg)) * xu) < TOL
