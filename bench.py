@@ -92,6 +92,8 @@ def parse_args():
     ap.add_argument("--tokens", type=str, default=None, help="comma list overriding the M sweep")
     ap.add_argument("--ratios", type=str, default=None, help="comma list overriding the ratio sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-row-parallel", action="store_true",
+                    help="linear sweep under torchrun: skip the row-parallel all-reduce check")
     ap.add_argument("--details", type=str, default=None, help="write per-layer results (JSON) here")
     ap.add_argument("--sweep-shapes", choices=["llama8b", "llama70b-tp8"], default="llama8b",
                     help="plan-sweep: the Llama-3-8B layers, or one TP8 rank's Llama-3-70B layers")
@@ -347,6 +349,133 @@ def linear_parity(torch, layers, calls, outputs, weights, x_dev, tol=1e-2):
             "checked": "rank 0, on the full (all-gathered) outputs of every layer call"}
 
 
+def row_parallel_check(torch, rank, world, steps=10, tol=1e-2):
+    """The row-parallel layers of a tensor-parallel decoder (o and down of the
+    Llama-3-8B shapes), with input features sharded over the ranks and half of
+    each rank's output features in its pinned host memory.  Every rank's
+    partial y is summed over the ranks three ways: by the all-reduce fused into
+    the linear kernel (``dak_linear_split_allreduce``), by the linear followed
+    by an NCCL all-reduce, and, where NVSwitch multicast is available, by the
+    consumer-side reduction the decoder uses (publish-only linear, then
+    ``dak_rmsnorm_allreduce`` adds the sum to a residual and normalises).
+    Rank 0 checks each against torch F.linear in FP32 on the host cores on the
+    full weight, and every rank checks that its sum equals rank 0's.  Each way
+    is then timed per call: a CUDA graph of ``steps`` calls, max over ranks."""
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from directaccesskernel_b200 import runtime
+    from directaccesskernel_b200.tp import SymmetricAllReduce
+
+    shapes = {name: LLAMA8B[name] for name in ("o", "down")}
+    ntoks = (1, 32)
+    slot = max(ntoks) * max(n for n, _ in shapes.values())
+    ar = SymmetricAllReduce(slot_elems=slot)
+    arc = SymmetricAllReduce(slot_elems=slot, consumer_reduces=True)
+    g = torch.Generator(device="cuda").manual_seed(4321)  # the same draws on every rank
+    worst = {"fused_linear": 0.0, "linear_nccl": 0.0, "rmsnorm_residual": 0.0, "rmsnorm_out": 0.0,
+             "ranks_differ": 0.0}
+    calls = {}
+
+    def rel(a, b):
+        return ((a.float().cpu() - b.float()).abs().max() / b.float().abs().max()).item()
+
+    def same_as_rank0(t):
+        t0 = t.clone()
+        dist.broadcast(t0, 0)
+        return (t.float() - t0.float()).abs().max().item()
+
+    for name, (n, k) in shapes.items():
+        if k % world:
+            raise RuntimeError(f"{name}: {k} input features do not split over {world} ranks")
+        kr = k // world
+        w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).half()
+        wt = w[:, rank * kr:(rank + 1) * kr].t().contiguous()  # this rank's transposed shard [kr, n]
+        w_host = wt[:, :n // 2].cpu().pin_memory()
+        w_dev = wt[:, n // 2:].contiguous()
+        wn = (1 + 0.1 * torch.randn(n, generator=g, device="cuda")).half()
+        w_cpu = w.float().cpu() if rank == 0 else None
+        del w
+        for m in ntoks:
+            x = torch.randn(m, k, generator=g, device="cuda").half()
+            res = torch.randn(m, n, generator=g, device="cuda").half()
+            xr = x[:, rank * kr:(rank + 1) * kr].contiguous()
+            y = torch.empty(m, n, dtype=torch.float16, device="cuda")
+            y2 = torch.empty_like(y)
+            runtime.linear_split(xr, y, w_host, w_dev, allreduce=ar)
+            runtime.linear_split(xr, y2, w_host, w_dev)
+            dist.all_reduce(y2)
+            state, out = res.clone(), torch.empty_like(res)
+            if arc.publish_only:
+                yc = torch.empty_like(y)  # layout only: a publish-only call leaves it unwritten
+                runtime.linear_split(xr, yc, w_host, w_dev, allreduce=arc)
+                arc.rmsnorm(yc, state, wn, 1e-5, out)
+            torch.cuda.synchronize()
+            worst["ranks_differ"] = max(worst["ranks_differ"], same_as_rank0(y), same_as_rank0(state))
+            if rank == 0:
+                ref = F.linear(x.float().cpu(), w_cpu)
+                worst["fused_linear"] = max(worst["fused_linear"], rel(y, ref))
+                worst["linear_nccl"] = max(worst["linear_nccl"], rel(y2, ref))
+                if arc.publish_only:
+                    h = ref.half() + res.cpu()
+                    hf = h.float()
+                    o_ref = wn.cpu() * (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)).half()
+                    worst["rmsnorm_residual"] = max(worst["rmsnorm_residual"], rel(state, h))
+                    worst["rmsnorm_out"] = max(worst["rmsnorm_out"], rel(out, o_ref))
+            # timed with the whole shard in HBM, so the reduction is not hidden
+            # behind the host link
+            calls[(name, m)] = (xr, y, y2, None, wt, state, out, wn)
+
+    # ---- per-call device time of each way, at 32 tokens (a decode batch), with
+    # each rank's shard all in HBM
+    stream = torch.cuda.current_stream()
+    ways = {"fused_linear": lambda c: runtime.linear_split(c[0], c[1], c[3], c[4], allreduce=ar),
+            "linear_nccl": lambda c: (runtime.linear_split(c[0], c[2], c[3], c[4]), dist.all_reduce(c[2]))}
+    if arc.publish_only:
+        ways["consumer_rmsnorm"] = lambda c: (runtime.linear_split(c[0], c[1], c[3], c[4], allreduce=arc),
+                                              arc.rmsnorm(c[1], c[5], c[7], 1e-5, c[6]))
+    us = {}
+    for way, fn in ways.items():
+        for name in shapes:
+            c = calls[(name, 32)]
+            for _ in range(3):
+                fn(c)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(steps):
+                    fn(c)
+            graph.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us[f"{way}/{name}"] = e0.elapsed_time(e1) * 1e3 / steps
+            del graph  # graphs that hold NCCL calls go before the process group
+    torch.cuda.synchronize()
+    status = runtime.device_status()
+    t = torch.tensor(list(us.values()) + [float(status != 0)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = dict(zip(us, [round(v, 2) for v in t.tolist()[:-1]]))
+    errs = torch.tensor(list(worst.values()), dtype=torch.float64, device="cuda")
+    dist.all_reduce(errs, op=dist.ReduceOp.MAX)
+    worst = dict(zip(worst, [round(v, 6) for v in errs.tolist()]))
+    checked = ["fused_linear", "linear_nccl"] + (["rmsnorm_residual", "rmsnorm_out"] if arc.publish_only else [])
+    return {"layers": {name: f"[{n} x {k}] split over {world} ranks by input feature" for name, (n, k) in shapes.items()},
+            "tokens": list(ntoks), "mode": ar.mode, "consumer_side": arc.publish_only,
+            "max_rel_err": {key: worst[key] for key in checked},
+            "max_abs_diff_between_ranks": worst["ranks_differ"],
+            "tolerance": tol,
+            "ok": all(worst[key] <= tol for key in checked) and worst["ranks_differ"] == 0.0 and t[-1].item() == 0,
+            "us_per_call_32_tokens": us,
+            "timing_basis": "each rank's whole shard in HBM; CUDA graph of 10 calls, events, max over ranks",
+            "reference": "torch F.linear(x.float(), W.float()) of the full weight on rank 0's host cores; "
+                         "RMSNorm of the 16-bit residual sum in FP32"}
+
+
 def run_linear(args, torch, rank, world):
     from directaccesskernel_b200 import runtime
 
@@ -521,6 +650,8 @@ def run_linear(args, torch, rank, world):
     torch.cuda.synchronize()
     parity = linear_parity(torch, layers, calls, outputs, weights, x_dev) if rank == 0 else None
     del outputs
+    # Under tensor parallelism, the row-parallel layers' all-reduce as well.
+    row_parallel = row_parallel_check(torch, rank, world) if tp and not args.no_row_parallel else None
 
     # ---- reduce over ranks (max time, summed bytes)
     w_bytes_step = sum(l["w_bytes"] for (l, m) in calls)
@@ -627,6 +758,8 @@ def run_linear(args, torch, rank, world):
     }
     if tp:
         line["tp"] = tp_info
+        if row_parallel is not None:
+            line["row_parallel"] = row_parallel
         line["roofline"]["nvlink_gbs"] = NVLINK_GBS
         line["roofline"]["host_link_basis"] = "each rank's own link, all ranks streaming at once"
     if cpu is not None:
