@@ -751,8 +751,8 @@ def run_linear(args, torch, rank, world):
                 "method": "per step: one copy of the step's distinct activations from pinned host memory, every "
                           "layer through the module API (eager), every layer's output read back to pinned host "
                           "memory on a side stream as soon as the layer is done"},
-        "gpu_launches": world * sum(-(-m // (2 * MMA_MAX_TOKENS if l["host_bytes"] and m > MMA_MAX_TOKENS
-                                             else MMA_MAX_TOKENS)) for (l, m) in calls) * args.steps,
+        "gpu_launches": world * sum(-(-m // (2 * MMA_MAX_TOKENS if m > MMA_MAX_TOKENS else MMA_MAX_TOKENS))
+                                    for (l, m) in calls) * args.steps,
         "clocks": clock,
         "parity": parity,
     }

@@ -544,11 +544,17 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
   const int max_ks = mma ? kMmaMaxKsplitHost : kCoreMaxKsplit;
   const int nkb = (int)((a->K + bk - 1) / bk);
 
-  // Token chunks: the tcgen05 kernel serves up to 256 tokens per launch; the
+  // Token chunks: the tcgen05 kernel serves up to 256 tokens per grid row; the
   // wide kernel up to 512 for a layer with host-resident rows, so that those
-  // rows cross the host link once per 512 tokens instead of once per 256.
+  // rows cross the host link once per 512 tokens instead of once per 256.  An
+  // HBM-only layer also takes up to 512 tokens per launch, as grid rows of 64
+  // to 256 tokens (token slices, planned below), so that each weight tile is
+  // brought into shared memory once per 512 tokens at about the same time by
+  // every row, not once per 256-token launch.
   const bool wide = mma && !ar && !glu && a->host_cols > 0 && a->ntok > kMmaMaxTok;
-  const int64_t chunk = wide ? 2 * kMmaMaxTok : mma ? kMmaMaxTok : kCoreMaxTok;
+  const bool sliced = mma && !ar && !glu && a->host_cols == 0 && a->ntok > kMmaMaxTok && a->host_ctas <= 0 &&
+                      a->dev_ctas <= 0;
+  const int64_t chunk = (wide || sliced) ? 2 * kMmaMaxTok : mma ? kMmaMaxTok : kCoreMaxTok;
   for (int64_t t0 = 0; t0 < a->ntok; t0 += chunk) {
     const int64_t nt = std::min(chunk, a->ntok - t0);
     if (wide && nt > kMmaMaxTok) {
@@ -558,7 +564,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
     int tmpl = 1;
     if (mma) {
       tmpl = 16;
-      while (tmpl < nt) tmpl *= 2;
+      while (tmpl < nt && tmpl < kMmaMaxTok) tmpl *= 2;  // a chunk above 256 tokens must take token rows
     } else {
       while (tmpl < nt) tmpl *= 2;
     }
@@ -658,6 +664,10 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
       // busiest CTA wins (by at least 5%); on the Llama-3-8B layers at 256
       // tokens this model orders the 1-, 2- and 4-row plans as their measured
       // times do.
+      // A chunk of more tokens than one row holds (257..512) always takes
+      // rows: the row width with the fewest operand bytes for its busiest
+      // CTA, 256 included.
+      const bool must_slice = nt > tmpl;
       if (mma && !ar && tiles_h == 0 && pd.ctas > 0 && pd.ksplit == 1 && tmpl >= 128) {
         const int boxes = (int)((a->dev_cols + kBoxCols - 1) / kBoxCols);
         const int bpt = bn / kBoxCols;
@@ -665,10 +675,10 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
           const int tiles = ((boxes + groups - 1) / groups + bpt - 1) / bpt;  // the busiest group's tiles
           return (long)tiles * (256 + 2 * w);
         };
-        long best_cost = busiest_cost(pd.ctas, tmpl);
+        long best_cost = must_slice ? -1 : busiest_cost(pd.ctas, tmpl);
         int best_w = 0, best_groups = 0, best_rows = 1;
         const int tiles_all = (boxes + bpt - 1) / bpt;
-        for (int sl = 2; sl <= 4 && tmpl / sl >= 64; sl *= 2) {
+        for (int sl = must_slice ? 1 : 2; sl <= 4 && tmpl / sl >= 64; sl *= 2) {
           const int w = tmpl / sl;
           const int rows = (int)((nt + w - 1) / w);
           const size_t sm = linear_mma_smem_bytes(w, 0);
@@ -679,7 +689,7 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
           const int per = (tiles_all + groups - 1) / groups;
           groups = (tiles_all + per - 1) / per;  // the fewest groups with that many tiles each
           const long cost = busiest_cost(groups, w);
-          if (20 * cost < 19 * best_cost) {
+          if (best_cost < 0 || 20 * cost < 19 * best_cost) {
             best_cost = cost;
             best_w = w;
             best_groups = groups;
@@ -693,6 +703,8 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
         }
       }
     }
+    if ((int64_t)std::max(1, tok_slices) * tmpl < nt)
+      return fail(DAK_ERR_UNSUPPORTED, "linear: no token-row plan covers %lld tokens", (long long)nt);
     const int span_h = (ph.ctas + cluster - 1) / cluster * cluster;
     const int span_d = (pd.ctas + cluster - 1) / cluster * cluster;
     const int grid = span_h + span_d;

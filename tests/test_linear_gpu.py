@@ -310,11 +310,12 @@ def test_config2_llama8b_sweep(name):
             assert rel_err(y, ref) < TOL, (name, m, r, rel_err(y, ref))
 
 
-@pytest.mark.parametrize("ntok", [65, 128, 200, 256, 512])
+@pytest.mark.parametrize("ntok", [65, 128, 200, 256, 300, 512, 700, 1024])
 @pytest.mark.parametrize("name", list(LLAMA8B))
 def test_token_sliced_hbm_only_prefill(name, ntok):
-    """HBM-only layers above 64 tokens run as grid rows of 64 or 128 tokens
-    (ragged last row included); every row writes only its own tokens."""
+    """HBM-only layers above 64 tokens run as grid rows of 64 to 256 tokens,
+    up to 512 tokens per launch (ragged last row and ragged last launch
+    included); every row writes only its own tokens."""
     n, k = LLAMA8B[name]
     g = torch.Generator().manual_seed(ntok)
     w = (torch.randn(n, k, generator=g) * 0.02).half()
@@ -339,8 +340,9 @@ def test_hbm_only_multi_tile_ctas(n_out, k, ntok):
 
 def test_token_slices_are_planned(tmp_path):
     """The plan trace shows the narrow HBM-only layer of 4096 features cut into
-    four 64-token rows at 256 tokens, no rows when it has host rows, and a wide
-    HBM-only layer (224 tiles) left whole."""
+    four 64-token rows at 256 tokens and into four 128-token rows of one launch
+    at 512 tokens, no rows when it has host rows, and a wide HBM-only layer
+    (224 tiles) left whole at 256 tokens."""
     import os
     import subprocess
     import sys
@@ -357,6 +359,8 @@ def test_token_slices_are_planned(tmp_path):
         "runtime.linear_split(x, y, w[:, :512].contiguous().pin_memory(), w[:, 512:].contiguous().cuda(), 0, 512)\n"
         "wide = (torch.randn(1024, 28672, device='cuda') * 0.02).half()\n"
         "runtime.linear_split(x, torch.empty(256, 28672, device='cuda').half(), None, wide)\n"
+        "x2 = torch.randn(512, 1024, device='cuda').half()\n"
+        "runtime.linear_split(x2, torch.empty(512, 4096, device='cuda').half(), None, w.cuda())\n"
         "torch.cuda.synchronize()\n"
         "assert runtime.device_status() == 0\n")
     env = dict(os.environ, DAK_B200_TRACE_PLAN="1", PYTHONPATH=str(REPO))
@@ -367,6 +371,9 @@ def test_token_slices_are_planned(tmp_path):
     assert "x 4 rows of 64 tokens |" in plans[0], plans[0]
     assert "x 1 rows of 256 tokens |" in plans[1], plans[1]
     assert "x 1 rows of 256 tokens |" in plans[2], plans[2]
+    # 512 tokens of the narrow layer: one launch of four 128-token rows.
+    wide_plans = [line for line in r.stderr.splitlines() if line.startswith("[dak plan] tcgen05 ntok=512")]
+    assert len(wide_plans) == 1 and "x 4 rows of 128 tokens |" in wide_plans[0], r.stderr
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
