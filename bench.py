@@ -308,8 +308,9 @@ def linear_metric_config(prefill, tokens, ratios, world):
     """Metric name and `config` of the linear workloads, the same for both arms."""
     if prefill:
         metric = f"offloaded linear effective weight GB/s (Llama-3-8B layers, prefill M={tokens})"
-        workload = (f"large-N prefill: Llama-3-8B qkv/o/gate_up/down x M{tokens} x r{ratios}; up to 512 tokens "
-                    f"per launch for layers with host rows, {MMA_MAX_TOKENS} otherwise")
+        workload = (f"large-N prefill: Llama-3-8B qkv/o/gate_up/down x M{tokens} x r{ratios}; up to "
+                    f"{2 * MMA_MAX_TOKENS} tokens per launch (HBM-only layers as grid rows of up to "
+                    f"{MMA_MAX_TOKENS} tokens)")
     else:
         metric = "offloaded GEMV effective weight GB/s (Llama-3-8B linear sweep)"
         workload = "BASELINE config 2: Llama-3-8B qkv/o/gate_up/down x M{1,4,16,64} x r{0,.25,.5,.75,1}"
