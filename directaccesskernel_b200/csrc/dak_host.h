@@ -84,10 +84,13 @@ cudaError_t launch_linear_mma(const LinearParams &p, int ntok_tmpl, int dtype, i
 // The wide tcgen05 kernel: 257..512 tokens per launch, each weight tile
 // streamed once for both 256-token halves; no split-K, no clusters.  Its
 // weight tile maps use boxes of 64 features x linear_wide_k_rows() K rows and
-// its activation map boxes of 64 K x 256 tokens.
-size_t linear_wide_smem_bytes();
+// its activation map boxes of 64 K x 256 tokens.  With `pair`, each CTA
+// instead applies one 256-token row of the batch (grid row, p.tok_slices
+// rows) to two 128-feature tiles at once.
+size_t linear_wide_smem_bytes(bool pair);
 int linear_wide_k_rows();
-cudaError_t launch_linear_wide(const LinearParams &p, int dtype, int grid, size_t smem, cudaStream_t stream);
+cudaError_t launch_linear_wide(const LinearParams &p, int dtype, int grid, size_t smem, cudaStream_t stream,
+                               bool pair = false);
 // Batches above 256 tokens of a layer with host-resident rows go to the wide
 // kernel in chunks of up to 512 tokens.
 

@@ -14,6 +14,16 @@
 // accumulators that together fill the SM's 512 TMEM columns.  Token t of the
 // batch is accumulator column t.
 //
+// Paired mode (PAIR = true), for HBM-only layers wide enough to fill the SMs:
+// the roles of the two operands swap.  A CTA owns two 128-feature tiles (four
+// 64-feature boxes) and one 256-token row of the batch (grid row
+// blockIdx.y), and applies each activation stage to both weight tiles: per
+// 64-row K stage it loads four 8 KB weight boxes and one 32 KB activation box,
+// and issues UMMA 128 x 256 x 16 once per tile into two 256-column
+// accumulators.  Per K row of two tiles it moves 512 bytes of weights and 512
+// of activations, where two separate tiles of the 256-token kernel move 512
+// and 1024.  Three stages (64 KB each) fit.
+//
 // Roles (192 threads) as in the 256-token kernel: warp 0 issues TMA loads,
 // warp 1 owns TMEM and issues the MMAs, warps 2..5 read the accumulators back
 // (each its TMEM lane quadrant) and store the 16-bit output.  No split-K and
@@ -32,30 +42,36 @@ namespace {
 
 constexpr int kWideBK = 64;                                   // K rows per stage (4 UMMA K-steps)
 constexpr int kWideHalf = 256;                                // tokens per accumulator (UMMA N)
-constexpr int kWideStages = 2;
 constexpr uint32_t kWideWBox = kBoxCols * kWideBK * 2;        // 8 KB: 64 features x 64 K rows
-constexpr uint32_t kWideWStage = 2 * kWideWBox;               // 16 KB
 constexpr uint32_t kWideXBox = kWideHalf * kWideBK * 2;       // 32 KB: 256 tokens x 64 K
-constexpr uint32_t kWideXStage = 2 * kWideXBox;               // 64 KB
 constexpr uint32_t kWideTmemCols = 2 * kWideHalf;             // 512: the whole TMEM
-constexpr int kWideBoxesPerTile = kMmaBM / kBoxCols;          // 2
 
+// Per mode: weight boxes and activation boxes per stage, and the stage count.
+template <bool PAIR>
 struct WideLayout {
+  static constexpr int stages = PAIR ? 3 : 2;
+  static constexpr int w_boxes = PAIR ? 4 : 2;                // 64-feature boxes per tile (the CTA's unit)
+  static constexpr int x_boxes = PAIR ? 1 : 2;                // 256-token activation boxes per stage
+  static constexpr uint32_t w_stage = w_boxes * kWideWBox;    // 32 KB / 16 KB
+  static constexpr uint32_t x_stage = x_boxes * kWideXBox;    // 32 KB / 64 KB
   static constexpr uint32_t w_off = 0;
-  static constexpr uint32_t x_off = w_off + kWideStages * kWideWStage;
-  static constexpr uint32_t bar_off = x_off + kWideStages * kWideXStage;
+  static constexpr uint32_t x_off = w_off + stages * w_stage;
+  static constexpr uint32_t bar_off = x_off + stages * x_stage;
   // full[S], empty[S], tmem_full, tmem_empty, last_done
-  static constexpr uint32_t misc_off = bar_off + (2 * kWideStages + 3) * 8;  // tmem slot, abort flags
-  static constexpr uint32_t bytes = misc_off + 16 + 1024;                     // + alignment slack
+  static constexpr uint32_t misc_off = bar_off + (2 * stages + 3) * 8;  // tmem slot, abort flags
+  static constexpr uint32_t bytes = misc_off + 16 + 1024;                // + alignment slack
 };
-static_assert(WideLayout::bytes <= 227 * 1024, "two wide stages must fit one CTA's shared memory");
-static_assert(WideLayout::x_off % 1024 == 0 && kWideXBox % 1024 == 0 && kWideWBox % 1024 == 0,
+static_assert(WideLayout<false>::bytes <= 227 * 1024 && WideLayout<true>::bytes <= 227 * 1024,
+              "the wide stages must fit one CTA's shared memory");
+static_assert(WideLayout<false>::x_off % 1024 == 0 && WideLayout<true>::x_off % 1024 == 0 &&
+                  kWideXBox % 1024 == 0 && kWideWBox % 1024 == 0,
               "128-byte-swizzled operand tiles start on 1024-byte boundaries");
 
-template <typename T>
+template <typename T, bool PAIR>
 __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __grid_constant__ LinearParams p) {
-  using L = WideLayout;
-  constexpr int S = kWideStages;
+  using L = WideLayout<PAIR>;
+  constexpr int S = L::stages;
+  constexpr int kWideBoxesPerTile = L::w_boxes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
@@ -73,6 +89,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __gri
   auto tile_box0 = [&](int j) { return work.box_begin + j * kWideBoxesPerTile; };
   auto tile_nbox = [&](int j) { return min(kWideBoxesPerTile, work.box_end - tile_box0(j)); };
   const int nkb = (p.K + kWideBK - 1) / kWideBK;
+  // Paired mode: this CTA's 256-token row of the batch.
+  const int tok0 = PAIR ? (int)blockIdx.y * kWideHalf : 0;
 
   const uint32_t full0 = sbase + L::bar_off;
   const uint32_t empty0 = full0 + S * 8;
@@ -114,17 +132,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __gri
       auto w_loads = [&](int i, uint32_t fb) {
         const int j = i / nkb, kb = i % nkb;
         const int nbox = tile_nbox(j);
-        mbar_arrive_expect_tx(fb, (uint32_t)nbox * kWideWBox + kWideXStage);
-        const uint32_t wdst = sbase + L::w_off + (i % S) * kWideWStage;
+        mbar_arrive_expect_tx(fb, (uint32_t)nbox * kWideWBox + L::x_stage);
+        const uint32_t wdst = sbase + L::w_off + (i % S) * L::w_stage;
         for (int bx = 0; bx < nbox; ++bx)
           tma_load_2d(wdst + bx * kWideWBox, &tier.wmap, (tile_box0(j) + bx) * kBoxCols, kb * kWideBK, fb, pol_w);
       };
       auto x_load = [&](int i, uint32_t fb) {
-        const uint32_t xdst = sbase + L::x_off + (i % S) * kWideXStage;
-        // Rows past the batch read as zeros (tile-map bounds), so both halves
-        // always carry full boxes.
-        for (int h = 0; h < 2; ++h)
-          tma_load_2d(xdst + h * kWideXBox, &p.xmap, (i % nkb) * kWideBK, h * kWideHalf, fb, pol_x);
+        const uint32_t xdst = sbase + L::x_off + (i % S) * L::x_stage;
+        // Rows past the batch read as zeros (tile-map bounds), so every box
+        // is full.
+        for (int h = 0; h < L::x_boxes; ++h)
+          tma_load_2d(xdst + h * kWideXBox, &p.xmap, (i % nkb) * kWideBK, tok0 + h * kWideHalf, fb, pol_x);
       };
       // Weights do not depend on the previous kernel of the stream.
       const int pre = p.pdl ? min(total, S) : 0;
@@ -160,6 +178,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __gri
       int s = 0;
       uint32_t ph = 0;
       for (int j = 0; j < ntiles; ++j) {
+        // Paired mode: a last unit of one or two boxes leaves the second
+        // accumulator without weights.
+        const int halves = PAIR ? (tile_nbox(j) > 2 ? 2 : 1) : 2;
         // Wait until the epilogue has read the previous tile's accumulators.
         mbar_wait<false>(tempty, ((uint32_t)j & 1u) ^ 1u, wc);
         tc_fence_after();
@@ -168,17 +189,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __gri
           tc_fence_after();
           if (lane == 0) {
             if (ok) {
-              const uint32_t wst = sbase + L::w_off + s * kWideWStage;
-              const uint32_t xst = sbase + L::x_off + s * kWideXStage;
+              const uint32_t wst = sbase + L::w_off + s * L::w_stage;
+              const uint32_t xst = sbase + L::x_off + s * L::x_stage;
 #pragma unroll
               for (int kk = 0; kk < kWideBK / 16; ++kk) {
-                // A: MN-major SW128; 16 K rows = 2 KB; LBO = next 64-feature box, SBO = 8 rows.
-                const uint64_t ad = smem_desc_sw128(wst + kk * 2048, kWideWBox, 1024);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                  // B: K-major SW128; 16 K = 32 B inside the 128-byte span; SBO = 8 rows.
-                  const uint64_t bd = smem_desc_sw128(xst + h * kWideXBox + kk * 32, 16, 1024);
-                  tc_mma_f16(tmem_base + (uint32_t)(h * kWideHalf), ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                  if (h < halves) {
+                    // A: MN-major SW128; 16 K rows = 2 KB; LBO = next 64-feature box, SBO = 8 rows.
+                    // Paired mode: accumulator h takes the tile of boxes 2h and 2h + 1.
+                    const uint64_t ad =
+                        smem_desc_sw128(wst + (PAIR ? h * 2 * kWideWBox : 0u) + kk * 2048, kWideWBox, 1024);
+                    // B: K-major SW128; 16 K = 32 B inside the 128-byte span; SBO = 8 rows.
+                    // Unpaired: accumulator h takes token half h.
+                    const uint64_t bd = smem_desc_sw128(xst + (PAIR ? 0u : h * kWideXBox) + kk * 32, 16, 1024);
+                    tc_mma_f16(tmem_base + (uint32_t)(h * kWideHalf), ad, bd, idesc,
+                               (kb > 0 || kk > 0) ? 1u : 0u);
+                  }
                 }
               }
             }
@@ -212,17 +239,27 @@ __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __gri
       for (int j = 0; j < ntiles; ++j) {
         mbar_wait<false>(tfull, (uint32_t)j & 1u, wc);
         tc_fence_after();
-        const int col = tile_box0(j) * kBoxCols + f;
-        const bool col_ok = f < tile_nbox(j) * kBoxCols && col < tier.cols;
-        uint16_t *ycol = reinterpret_cast<uint16_t *>(p.y) + tier.col_offset + col;
+        // Unpaired: one 128-feature tile, token t in accumulator column t (both
+        // accumulators).  Paired: accumulator h holds features [128h, 128h + 128)
+        // of the unit for the CTA's token row.
+        const int nfeat = tile_nbox(j) * kBoxCols;
+        const int nacc = PAIR ? (tile_nbox(j) > 2 ? 2 : 1) : 1;
+        const int ntok_here = PAIR ? min(kWideHalf, p.ntok - tok0) : p.ntok;  // warp-uniform
+        for (int h = 0; h < nacc; ++h) {
+          const int fo = (PAIR ? h * kMmaBM : 0) + f;
+          const int col = tile_box0(j) * kBoxCols + fo;
+          const bool col_ok = fo < nfeat && col < tier.cols;
+          uint16_t *ycol = reinterpret_cast<uint16_t *>(p.y) + (long long)tok0 * p.ldy + tier.col_offset + col;
+          const uint32_t acc = PAIR ? (uint32_t)(h * kWideHalf) : 0u;
 #pragma unroll 1
-        for (int c0 = 0; c0 < p.ntok; c0 += 32) {  // warp-uniform bound
-          float v[32];
-          tmem_ld32(tmem_base + lane_addr + (uint32_t)c0, v);
-          if (col_ok) {
+          for (int c0 = 0; c0 < ntok_here; c0 += 32) {
+            float v[32];
+            tmem_ld32(tmem_base + lane_addr + acc + (uint32_t)c0, v);
+            if (col_ok) {
 #pragma unroll
-            for (int t = 0; t < 32; ++t)
-              if (c0 + t < p.ntok) ycol[(long long)(c0 + t) * p.ldy] = Elem<T>::from_float(v[t]);
+              for (int t = 0; t < 32; ++t)
+                if (c0 + t < ntok_here) ycol[(long long)(c0 + t) * p.ldy] = Elem<T>::from_float(v[t]);
+            }
           }
         }
         tc_fence_before();
@@ -240,15 +277,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1) linear_wide_kernel(const __gri
 
 }  // namespace
 
-size_t linear_wide_smem_bytes() { return WideLayout::bytes; }
+size_t linear_wide_smem_bytes(bool pair) { return pair ? WideLayout<true>::bytes : WideLayout<false>::bytes; }
 
 int linear_wide_k_rows() { return kWideBK; }
 
-cudaError_t launch_linear_wide(const LinearParams &p, int dtype, int grid, size_t smem, cudaStream_t stream) {
+cudaError_t launch_linear_wide(const LinearParams &p, int dtype, int grid, size_t smem, cudaStream_t stream,
+                               bool pair) {
   if (dtype == DAK_DTYPE_F16)
-    return launch_linear_kernel(linear_wide_kernel<__half>, p, grid, kMmaThreads, 1, smem, stream, nullptr);
+    return pair ? launch_linear_kernel(linear_wide_kernel<__half, true>, p, grid, kMmaThreads, 1, smem, stream, nullptr)
+                : launch_linear_kernel(linear_wide_kernel<__half, false>, p, grid, kMmaThreads, 1, smem, stream,
+                                       nullptr);
   if (dtype == DAK_DTYPE_BF16)
-    return launch_linear_kernel(linear_wide_kernel<__nv_bfloat16>, p, grid, kMmaThreads, 1, smem, stream, nullptr);
+    return pair ? launch_linear_kernel(linear_wide_kernel<__nv_bfloat16, true>, p, grid, kMmaThreads, 1, smem,
+                                       stream, nullptr)
+                : launch_linear_kernel(linear_wide_kernel<__nv_bfloat16, false>, p, grid, kMmaThreads, 1, smem,
+                                       stream, nullptr);
   return cudaErrorInvalidValue;
 }
 

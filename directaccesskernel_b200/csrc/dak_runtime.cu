@@ -448,12 +448,17 @@ int check_ptr16(const void *p, const char *what) {
 // the SMs (one CTA per SM: the kernel takes about 161 KB of shared memory).
 constexpr int kWideHostCtas = 32;
 
+// With pair_groups > 0 (an HBM-only layer), the paired mode instead: that many
+// CTAs per 256-token row of the chunk, each applying its row to two
+// 128-feature tiles at a time.
 int run_linear_wide_chunk(const dak_linear_args *a, const DeviceInfo *dev, int64_t t0, int64_t nt,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, int pair_groups = 0) {
+  const bool pair = pair_groups > 0;
   const int boxes_h = (int)((a->host_cols + kBoxCols - 1) / kBoxCols);
   const int boxes_d = (int)((a->dev_cols + kBoxCols - 1) / kBoxCols);
+  if (pair && boxes_h > 0) return fail(DAK_ERR_INVALID_ARG, "paired wide linear: the layer has host rows");
   const int hc = boxes_h > 0 ? std::max(1, std::min({kWideHostCtas, boxes_h, dev->num_sms / 2})) : 0;
-  const int dc = boxes_d > 0 ? std::max(1, std::min(dev->num_sms - hc, boxes_d)) : 0;
+  const int dc = pair ? pair_groups : boxes_d > 0 ? std::max(1, std::min(dev->num_sms - hc, boxes_d)) : 0;
   const int64_t tiers_cols[2] = {a->host_cols, a->dev_cols};
   const void *tiers_w[2] = {a->w_host, a->w_dev};
   const int64_t tiers_ld[2] = {a->ld_host, a->ld_dev};
@@ -482,13 +487,45 @@ int run_linear_wide_chunk(const dak_linear_args *a, const DeviceInfo *dev, int64
   p.K = (int)a->K;
   p.status = dev->status;
   p.pdl = pdl_enabled() ? 1 : 0;
-  const size_t smem = linear_wide_smem_bytes();
+  p.tok_slices = pair ? (int)((nt + kMmaMaxTok - 1) / kMmaMaxTok) : 0;
+  const size_t smem = linear_wide_smem_bytes(pair);
   if ((int)smem > dev->max_smem_optin) return fail(DAK_ERR_UNSUPPORTED, "wide linear: shared memory plan too large");
   if (trace_plans())
-    fprintf(stderr, "[dak plan] wide ntok=%lld K=%lld host_cols=%lld dev_cols=%lld | host ctas=%d | dev ctas=%d\n",
-            (long long)nt, (long long)a->K, (long long)a->host_cols, (long long)a->dev_cols, hc, dc);
-  const cudaError_t e = launch_linear_wide(p, a->dtype, hc + dc, smem, stream);
+    fprintf(stderr, "[dak plan] wide%s ntok=%lld K=%lld host_cols=%lld dev_cols=%lld | host ctas=%d | dev ctas=%d"
+            " x %d rows\n", pair ? " paired" : "", (long long)nt, (long long)a->K, (long long)a->host_cols,
+            (long long)a->dev_cols, hc, dc, std::max(1, p.tok_slices));
+  const cudaError_t e = launch_linear_wide(p, a->dtype, hc + dc, smem, stream, pair);
   return e == cudaSuccess ? DAK_OK : cuda_status(e, "wide linear kernel launch");
+}
+
+// Paired wide plan for an HBM-only chunk of 257..512 tokens: the CTAs per
+// 256-token row, or 0 when token rows of the tcgen05 kernel move fewer
+// operand bytes.  Both plans are costed as the token-row planner costs its
+// own: the bytes the busiest CTA brings into shared memory per K row.  A
+// paired unit (two 128-feature tiles, 256 tokens) brings 512 bytes of weights
+// and 512 of activations; a 128-feature tile of w tokens, 256 and 2w.  Both
+// kernels keep one CTA per SM.
+int paired_wide_groups(const dak_linear_args *a, const DeviceInfo *dev, int64_t nt) {
+  if (a->dev_cols <= 0 || a->host_cols > 0 || nt <= kMmaMaxTok || nt > 2 * kMmaMaxTok) return 0;
+  if ((int)linear_wide_smem_bytes(true) > dev->max_smem_optin) return 0;
+  const int cap = dev->num_sms;
+  const int boxes = (int)((a->dev_cols + kBoxCols - 1) / kBoxCols);
+  auto busiest = [&](int units, int rows, long unit_bytes, int *groups_out) -> long {
+    int groups = std::min(units, cap / rows);
+    if (groups <= 0) return -1;
+    const int per = (units + groups - 1) / groups;
+    if (groups_out) *groups_out = (units + per - 1) / per;
+    return (long)per * unit_bytes;
+  };
+  int groups = 0;
+  const long pair_cost = busiest((boxes + 3) / 4, 2, 1024, &groups);
+  if (pair_cost < 0) return 0;
+  long best_rows = -1;
+  for (int w = kMmaMaxTok; w >= 64; w /= 2) {
+    const long c = busiest((boxes + 1) / 2, (int)((nt + w - 1) / w), 256 + 2 * w, nullptr);
+    if (c >= 0 && (best_rows < 0 || c < best_rows)) best_rows = c;
+  }
+  return (best_rows < 0 || 20 * pair_cost < 19 * best_rows) ? groups : 0;
 }
 
 int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar = nullptr, bool glu = false) {
@@ -560,6 +597,13 @@ int run_linear(const dak_linear_args *a, cudaStream_t stream, const ArParams *ar
     if (wide && nt > kMmaMaxTok) {
       if ((st = run_linear_wide_chunk(a, dev, t0, nt, stream))) return st;
       continue;
+    }
+    if (sliced && nt > kMmaMaxTok) {
+      const int pg = paired_wide_groups(a, dev, nt);
+      if (pg > 0) {
+        if ((st = run_linear_wide_chunk(a, dev, t0, nt, stream, pg))) return st;
+        continue;
+      }
     }
     int tmpl = 1;
     if (mma) {

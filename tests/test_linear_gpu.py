@@ -338,11 +338,26 @@ def test_hbm_only_multi_tile_ctas(n_out, k, ntok):
     assert rel_err(y, ref) < TOL, rel_err(y, ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("ntok", [257, 300, 512])
+@pytest.mark.parametrize("n_out,k", [(28672, 1024), (28864, 1024), (38464, 512), (20480 + 192, 640)])
+def test_paired_wide_hbm_only(n_out, k, ntok, dtype):
+    """HBM-only layers wide enough to fill the SMs take 257..512 tokens on the
+    wide kernel's paired mode: each CTA applies one 256-token row to two
+    128-feature tiles.  Box counts that leave a last unit of one to three
+    64-feature boxes, and a ragged last token row, included."""
+    w, x = _inputs(n_out, k, ntok, dtype=dtype, seed=n_out + ntok)
+    ref = _oracle(w, x)
+    y = _split_run(w, x, 0)
+    assert not np.isnan(y).any()
+    assert rel_err(y, ref) < TOL, rel_err(y, ref)
+
+
 def test_token_slices_are_planned(tmp_path):
     """The plan trace shows the narrow HBM-only layer of 4096 features cut into
     four 64-token rows at 256 tokens and into four 128-token rows of one launch
     at 512 tokens, no rows when it has host rows, and a wide HBM-only layer
-    (224 tiles) left whole at 256 tokens."""
+    (224 tiles) left whole at 256 tokens and paired at 512."""
     import os
     import subprocess
     import sys
@@ -361,6 +376,7 @@ def test_token_slices_are_planned(tmp_path):
         "runtime.linear_split(x, torch.empty(256, 28672, device='cuda').half(), None, wide)\n"
         "x2 = torch.randn(512, 1024, device='cuda').half()\n"
         "runtime.linear_split(x2, torch.empty(512, 4096, device='cuda').half(), None, w.cuda())\n"
+        "runtime.linear_split(x2, torch.empty(512, 28672, device='cuda').half(), None, wide)\n"
         "torch.cuda.synchronize()\n"
         "assert runtime.device_status() == 0\n")
     env = dict(os.environ, DAK_B200_TRACE_PLAN="1", PYTHONPATH=str(REPO))
@@ -374,6 +390,9 @@ def test_token_slices_are_planned(tmp_path):
     # 512 tokens of the narrow layer: one launch of four 128-token rows.
     wide_plans = [line for line in r.stderr.splitlines() if line.startswith("[dak plan] tcgen05 ntok=512")]
     assert len(wide_plans) == 1 and "x 4 rows of 128 tokens |" in wide_plans[0], r.stderr
+    # 512 tokens of the wide layer (224 tiles): the paired mode, 56 CTAs x 2 rows.
+    paired = [line for line in r.stderr.splitlines() if line.startswith("[dak plan] wide paired ntok=512")]
+    assert len(paired) == 1 and "dev ctas=56 x 2 rows" in paired[0], r.stderr
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
