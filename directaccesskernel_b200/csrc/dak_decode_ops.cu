@@ -227,12 +227,22 @@ __global__ void silu_mul_kernel(const void *gu, long long ld, void *out, int row
 // tensor-parallel group left in its own buffer (dak_linear_split_allreduce in
 // publish-only mode).  Thread 0 waits, bounded, until every rank published the
 // current call; then the row is read as sums over ranks with multimem.ld_reduce
-// through the buffer's multicast address, 8 independent reads per thread at a
-// time.  h = round16(round16(sum) + residual) is written back to the residual
+// through the buffer's multicast address, 8 columns per thread, issued before
+// any is used: as two 16-byte reads of 4 adjacent columns (VEC4, when the row
+// and buffer are 16-byte aligned) or as 8 single-column reads.  Every column
+// is summed over the ranks in FP32 by the switch either way.
+// h = round16(round16(sum) + residual) is written back to the residual
 // stream, and out = w * round16(h * rsqrt(mean(h^2) + eps)).
 __device__ __forceinline__ float mm_ld_reduce_add(const float *p) {
   float v;
   asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 mm_ld_reduce_add_v4(const float *p) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
   return v;
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
@@ -255,7 +265,7 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   return v;
 }
 
-template <typename T>
+template <typename T, bool VEC4>
 __global__ void __launch_bounds__(kArThreads) rmsnorm_ar_kernel(const float *mc, long long slot, long long ld,
                                                                 const int *epoch, const uint32_t *flags, int world,
                                                                 long long timeout_ns, int *status, void *res,
@@ -285,16 +295,35 @@ __global__ void __launch_bounds__(kArThreads) rmsnorm_ar_kernel(const float *mc,
   const bool ok = !fail_s;
   const float *src = mc + (long long)(e & 1u) * slot + row * ld;
   uint16_t *rrow = static_cast<uint16_t *>(res) + row * (long long)cols;
+  // Column of this thread's u-th value: 4 adjacent columns per 16-byte read
+  // (VEC4), else one column per read, threads adjacent.
+  auto col_of = [&](int u) {
+    return VEC4 ? c_lo + 4 * ((int)threadIdx.x + (u >> 2) * kArThreads) + (u & 3)
+                : c_lo + (int)threadIdx.x + u * kArThreads;
+  };
   float v[kArPerThread];
+  if (VEC4) {
+    // c_lo and c_hi are multiples of 4, so a group is wholly in or out.
 #pragma unroll
-  for (int u = 0; u < kArPerThread; ++u) {
-    const int c = c_lo + threadIdx.x + u * kArThreads;
-    v[u] = (ok && c < c_hi) ? mm_ld_reduce_add(src + c) : 0.f;
+    for (int g = 0; g < kArPerThread / 4; ++g) {
+      const int c = col_of(4 * g);
+      const float4 q = (ok && c < c_hi) ? mm_ld_reduce_add_v4(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * g] = q.x;
+      v[4 * g + 1] = q.y;
+      v[4 * g + 2] = q.z;
+      v[4 * g + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < kArPerThread; ++u) {
+      const int c = col_of(u);
+      v[u] = (ok && c < c_hi) ? mm_ld_reduce_add(src + c) : 0.f;
+    }
   }
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < kArPerThread; ++u) {
-    const int c = c_lo + threadIdx.x + u * kArThreads;
+    const int c = col_of(u);
     if (ok && c < c_hi) {
       const float h = r16<T>(r16<T>(v[u]) + ld1<T>(rrow, c));
       v[u] = h;
@@ -324,7 +353,7 @@ __global__ void __launch_bounds__(kArThreads) rmsnorm_ar_kernel(const float *mc,
   uint16_t *orow = static_cast<uint16_t *>(out) + row * (long long)cols;
 #pragma unroll
   for (int u = 0; u < kArPerThread; ++u) {
-    const int c = c_lo + threadIdx.x + u * kArThreads;
+    const int c = col_of(u);
     if (c < c_hi) st1<T>(orow, c, ld1<T>(w, c) * r16<T>(v[u] * inv));
   }
 }
@@ -419,15 +448,20 @@ extern "C" int dak_rmsnorm_allreduce(const dak_allreduce_args *ar, void *residua
     return fail(DAK_ERR_UNSUPPORTED, "rmsnorm_allreduce serves at most %d columns", kArCluster * kArThreads * kArPerThread);
   const int pdl = decode_pdl_enabled() ? 1 : 0;
   const dim3 grid((unsigned)rows * kArCluster), block(kArThreads);
+  // 16-byte multicast reads need every row start, every CTA's first column
+  // (cols / 8 apart) and both parity slots 16-byte aligned.
+  const bool vec4 = cols % (4 * kArCluster) == 0 && ld % 4 == 0 && ar->slot_elems % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(ar->mc_f32) & 15u) == 0;
+  auto launch = [&](auto kern) {
+    return launch_ex(kern, grid, block, 0, s, kArCluster, pdl, (const float *)ar->mc_f32, (long long)ar->slot_elems,
+                     (long long)ld, (const int *)ar->epoch, (const uint32_t *)ar->flags[ar->rank], ar->world, tns,
+                     status, residual, weight, out, cols, eps, pdl);
+  };
   cudaError_t e;
   if (dtype == DAK_DTYPE_F16)
-    e = launch_ex(rmsnorm_ar_kernel<__half>, grid, block, 0, s, kArCluster, pdl, (const float *)ar->mc_f32,
-                  (long long)ar->slot_elems, (long long)ld, (const int *)ar->epoch,
-                  (const uint32_t *)ar->flags[ar->rank], ar->world, tns, status, residual, weight, out, cols, eps, pdl);
+    e = vec4 ? launch(rmsnorm_ar_kernel<__half, true>) : launch(rmsnorm_ar_kernel<__half, false>);
   else
-    e = launch_ex(rmsnorm_ar_kernel<__nv_bfloat16>, grid, block, 0, s, kArCluster, pdl, (const float *)ar->mc_f32,
-                  (long long)ar->slot_elems, (long long)ld, (const int *)ar->epoch,
-                  (const uint32_t *)ar->flags[ar->rank], ar->world, tns, status, residual, weight, out, cols, eps, pdl);
+    e = vec4 ? launch(rmsnorm_ar_kernel<__nv_bfloat16, true>) : launch(rmsnorm_ar_kernel<__nv_bfloat16, false>);
   if (e != cudaSuccess) return cuda_status(e, "rmsnorm_allreduce launch");
   return cuda_status(cudaGetLastError(), "rmsnorm_allreduce launch");
 }

@@ -108,7 +108,7 @@ def test_fused_allreduce_matches_nccl(world, multicast, dtype):
     print("fused all-reduce modes:", {r: res[r][2] for r in res})
 
 
-def _consumer_worker(rank, world, port, q):
+def _consumer_worker(rank, world, port, q, N=4096):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -121,7 +121,7 @@ def _consumer_worker(rank, world, port, q):
         from directaccesskernel_b200 import runtime
         from directaccesskernel_b200.tp import SymmetricAllReduce
 
-        N, Kr = 4096, 1024
+        Kr = 1024
         ar = SymmetricAllReduce(slot_elems=64 * N, consumer_reduces=True)
         if not ar.publish_only:
             q.put((rank, "no multicast", 0, ar.mode))
@@ -152,9 +152,11 @@ def _consumer_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_consumer_side_reduction_in_rmsnorm():
+@pytest.mark.parametrize("N", [4096, 4104])
+def test_consumer_side_reduction_in_rmsnorm(N):
     """Publish-only linear + dak_rmsnorm_allreduce against linear + NCCL all-reduce
-    + residual add + RMSNorm; needs 2 GPUs with NVSwitch multicast."""
+    + residual add + RMSNorm; needs 2 GPUs with NVSwitch multicast.  4096
+    columns take the 16-byte multicast reads, 4104 the single-column ones."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -162,7 +164,7 @@ def test_consumer_side_reduction_in_rmsnorm():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_consumer_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_consumer_worker, args=(r, 2, port, q, N)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
