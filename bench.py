@@ -81,7 +81,8 @@ def parse_args():
                     help="llama70b on 1 GPU: build one rank of a TP-N decoder (heads, KV heads, FFN and vocabulary "
                          "divided by N) to profile its kernels on one GPU; there is no all-reduce")
     ap.add_argument("--nccl-allreduce", action="store_true",
-                    help="llama70b: NCCL all-reduce after o and down instead of the fused path")
+                    help="llama70b: NCCL all-reduce after o and down (by default the decoder times the fused "
+                         "reduction and NCCL at set-up and keeps the faster)")
     ap.add_argument("--no-balance", action="store_true",
                     help="llama70b: same host fraction on every rank (default: balanced by host bandwidth)")
     ap.add_argument("--host-fraction", type=float, default=None,
@@ -1264,7 +1265,10 @@ def run_llama70b(args, torch, rank, world):
     g = torch.Generator().manual_seed(3)
     dec.ids.copy_(torch.randint(0, shape.vocab, (B,), generator=g).cuda())
     build_s = time.perf_counter() - t0
-    dec.capture()
+    # With the fused reduction available, the decoder times one step each way
+    # (consumer-side reduction, linear + NCCL) and keeps the faster.
+    dec.capture(choose_allreduce=fused)
+    fused = dec.use_fused
     for _ in range(W):
         dec.step()
     torch.cuda.synchronize()
@@ -1348,6 +1352,7 @@ def run_llama70b(args, torch, rank, world):
                                   f"one rank of tp{emulated} on 1 GPU (its kernels and shapes, no all-reduce)",
                    "allreduce": "fused: row-parallel kernels publish, the next RMSNorm reduces over NVSwitch "
                                 "multicast" if fused else "NCCL",
+                   "allreduce_choice_ms": dec.allreduce_times_ms,
                    "l2": "tens of GB read per step exceed L2",
                    "timing": "CUDA events around K graph replays, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": round((host_step + dev_step) / (step_ms * 1e-3) / 1e9, 2),

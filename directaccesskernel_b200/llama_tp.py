@@ -140,6 +140,8 @@ class TPLlamaDecoder(nn.Module):
 
             ar = SymmetricAllReduce(batch * shape.hidden, group=group, dtype=dtype, consumer_reduces=True)
             self.ar = ar if ar.publish_only else None
+        self.use_fused = self.ar is not None  # which reduction forward_step uses (see ``capture``)
+        self.allreduce_times_ms = None
 
     # ------------------------------------------------------------- weights
     def _make_linear(self, w: torch.Tensor) -> nn.Module:
@@ -317,14 +319,14 @@ class TPLlamaDecoder(nn.Module):
         publish-only mode the sum over ranks is read here, inside the norm."""
         from .decode_ops import rmsnorm
 
-        if self.ar is not None and self.ar.publish_only:
+        if self.use_fused:
             return self.ar.rmsnorm(y, self.hidden, w, self.s.eps, self.x_buf)
         return rmsnorm(y, w, self.s.eps, residual=self.hidden, out=self.x_buf)
 
     def _row_parallel(self, mod: nn.Module, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """A row-parallel projection summed over the ranks: the fused kernel when
         enabled, else the local linear followed by an NCCL all-reduce."""
-        if self.ar is None:
+        if not self.use_fused:
             y = mod(x)
             self._all_reduce(y)
             return y
@@ -376,9 +378,9 @@ class TPLlamaDecoder(nn.Module):
                 decode_paged(self.q_buf, kdev, vdev, khost, vhost, self.block_table, self.seq_lens, scale,
                              self.split, out=self.attn_out, partial_o=self.partial_o, partial_ml=self.partial_ml,
                              max_seq_len=self.max_ctx, merge_counters=self.merge_counters)
-            with t("o" if self.ar is not None else "o+allreduce"):
+            with t("o" if self.use_fused else "o+allreduce"):
                 o = self._row_parallel(layer.o, self.attn_out.view(B, qd), self.o_buf)
-            with t("allreduce+norm" if self.ar is not None else "norm"):
+            with t("allreduce+norm" if self.use_fused else "norm"):
                 x = self._add_norm(o, layer.post_w)
             if self.fuse_glu:
                 with t("gate_up+silu"):
@@ -388,10 +390,10 @@ class TPLlamaDecoder(nn.Module):
                     gu = layer.gate_up(x)
                 with t("silu"):
                     act = silu_mul(gu, out=self.act_buf)
-            with t("down" if self.ar is not None else "down+allreduce"):
+            with t("down" if self.use_fused else "down+allreduce"):
                 dn = self._row_parallel(layer.down, act, self.dn_buf)
             nxt_w = self.layers[l + 1].in_w if l + 1 < len(self.layers) else self.final_w
-            with t("allreduce+norm" if self.ar is not None else "norm"):
+            with t("allreduce+norm" if self.use_fused else "norm"):
                 x = self._add_norm(dn, nxt_w)
         with t("lm_head"):
             logits = self.lm_head(x)[:, :max(1, self.vocab_valid)]
@@ -466,18 +468,56 @@ class TPLlamaDecoder(nn.Module):
         self.pos.add_(1)
 
     @torch.inference_mode()
-    def capture(self) -> None:
+    def capture(self, choose_allreduce: bool = False, trials: int = 5) -> None:
         """Captures one decode step plus the advance into a CUDA graph (after a warm-up
-        step whose KV writes and advance are undone)."""
+        step whose KV writes and advance are undone).
+
+        With ``choose_allreduce`` and the fused reduction available, the step is
+        captured both ways (consumer-side reduction, and linear + NCCL), each graph
+        is replayed ``trials`` times from the same position, and the one whose
+        slowest rank is faster is kept: which wins depends on the group size and
+        the box.  Every rank captures and replays both graphs in the same order.
+        ``allreduce_times_ms`` records the median replay time of each."""
         pos0, ids0 = self.pos.clone(), self.ids.clone()
-        self.forward_step()
-        torch.cuda.synchronize()
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+
+        def one_graph():
             self.forward_step()
-            self.advance()
-        self.pos.copy_(pos0)
-        self.ids.copy_(ids0)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.forward_step()
+                self.advance()
+            self.pos.copy_(pos0)
+            self.ids.copy_(ids0)
+            torch.cuda.synchronize()
+            return g
+
+        if not (choose_allreduce and self.ar is not None and self.world > 1):
+            self.graph = one_graph()
+            return
+        stream = torch.cuda.current_stream()
+        graphs, times = {}, {}
+        for fused in (True, False):
+            self.use_fused = fused
+            g = one_graph()
+            ms = []
+            for _ in range(trials + 1):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+                self.pos.copy_(pos0)  # every trial runs from the same position
+                self.ids.copy_(ids0)
+                torch.cuda.synchronize()
+                ms.append(e0.elapsed_time(e1))
+            graphs[fused] = g
+            times[fused] = sorted(ms[1:])[len(ms[1:]) // 2]
+        t = torch.tensor([times[True], times[False]], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        self.allreduce_times_ms = {"fused": float(t[0]), "nccl": float(t[1])}
+        self.use_fused = bool(t[0] <= t[1])
+        self.graph = graphs[self.use_fused]
+        graphs.clear()  # the other graph (it may hold NCCL work) goes now
         torch.cuda.synchronize()
 
     def step(self) -> None:
