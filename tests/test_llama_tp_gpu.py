@@ -146,3 +146,69 @@ def test_tp2_matches_transformers(fused):
         p.join(timeout=120)
     for r in range(2):
         assert isinstance(res[r], float) and res[r] <= TOL, res
+
+
+def _tp2_choice_worker(rank, port, q):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from directaccesskernel_b200 import runtime
+        from directaccesskernel_b200.llama_tp import LlamaShape, TPLlamaDecoder
+
+        cfg = _cfg()
+        hf = _hf(cfg, seed=9)
+        g = torch.Generator().manual_seed(4)
+        prompt = torch.randint(0, cfg.vocab_size, (2, 12), generator=g).cuda()
+        dec = TPLlamaDecoder(LlamaShape.from_config(cfg), batch=2, max_ctx=48, weight_offload=0.25,
+                             kv_host_fraction=0.5, fused_allreduce=True).load_hf(hf)
+        _teacher_forced(dec, prompt[:, :-1])
+        dec.ids.copy_(prompt[:, -1])
+        dec.set_positions(prompt.shape[1] - 1)
+        dec.capture(choose_allreduce=True)
+        toks = []
+        for _ in range(6):
+            dec.step()
+            toks.append(dec.ids.clone())
+        got = torch.stack(toks, 1)
+        with torch.inference_mode():
+            ref = hf.generate(prompt, max_new_tokens=6, do_sample=False, min_new_tokens=6)[:, prompt.shape[1]:]
+        agree = (got == ref).float().mean().item()
+        q.put((rank, (agree, dec.use_fused, dec.allreduce_times_ms, dec.ar is not None, runtime.device_status())))
+        dec.release()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_chosen_reduction_continues_greedy_decode():
+    """capture(choose_allreduce=True) times the step with the consumer-side
+    reduction and with linear + NCCL, keeps the faster on both ranks alike, and
+    the kept graph continues greedy decode as transformers does."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp2_choice_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert isinstance(res[r], tuple), res
+        agree, use_fused, times, has_fused, status = res[r]
+        assert agree >= 0.8 and status == 0, res
+        if has_fused:  # both ways were timed; the choice follows the slower rank's times
+            assert times is not None and use_fused == (times["fused"] <= times["nccl"]), res
+        else:
+            assert times is None and not use_fused, res
+    assert res[0][1] == res[1][1], res  # the ranks kept the same reduction
