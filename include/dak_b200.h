@@ -80,7 +80,8 @@ typedef struct dak_constants {
   int tile_m;        /* output-feature granularity of the split (64)          */
   int tile_k;        /* K rows per pipeline stage                            */
   int mma_tile_m;    /* output features per tensor-core tile (128)           */
-  int mma_max_tokens;/* largest token count of one tensor-core launch (256)  */
+  int mma_max_tokens;/* tokens per tensor-core tile (UMMA N; 256); a launch  */
+                     /* may cover up to twice as many as rows of tiles     */
   int abi_version;
 } dak_constants;
 DAK_API int dak_get_constants(dak_constants *out);
