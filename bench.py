@@ -989,14 +989,15 @@ class CpuLinearSweep:
                 f"the ratio), weights built before timing, {self.threads} threads; GB/s of fp16 weight bytes")
 
 
-def cpu_baseline_linear(tokens, ratios, passes: int = 3):
+def cpu_baseline_linear(tokens, ratios, passes: int = 3, warmup: int = 3):
     """cpu_baseline of the GPU arm: the median of whole timed passes of the
-    reference's computation (torch F.linear, FP32) on all host cores, with the
-    oracle port's figure beside it."""
+    reference's computation (torch F.linear, FP32) on all host cores, after
+    ``warmup`` untimed passes (as the reference arm takes), with the oracle
+    port's figure beside it."""
     out = {}
     for impl in ("torch", "port"):
         sweep = CpuLinearSweep(tokens, ratios, impl)
-        times = sweep.timed_passes(passes)
+        times = sweep.timed_passes(passes, warmup=warmup)
         out[impl] = (sweep.bytes_per_pass / statistics.median(times) / 1e9, sweep, len(times))
         del sweep
     v, sweep, n = out["torch"]
@@ -1509,7 +1510,8 @@ def run_reference(args):
     t0 = time.perf_counter()
     times = sweep.timed_passes(args.steps, warmup=args.warmup)
     elapsed = time.perf_counter() - t0
-    v = round(sweep.bytes_per_pass * len(times) / sum(times) / 1e9, 3)
+    # The median pass, as the GPU arm's cpu_baseline reports it.
+    v = round(sweep.bytes_per_pass / statistics.median(times) / 1e9, 3)
     sample, threads = sweep.sample(), sweep.threads
     del sweep
     port = CpuLinearSweep(tokens, ratios, "port")
@@ -1524,7 +1526,7 @@ def run_reference(args):
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic N(0,0.02) weights, N(0,1) activations",
         "config": config,
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "reference",
-                         "sample": sample + f"; {len(times)} timed steps, one pass per step",
+                         "sample": sample + f"; median of {len(times)} timed steps, one pass per step",
                          "port_value": port_v, "port_kind": "port (numpy oracle, same passes)"},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": round(elapsed, 2),
